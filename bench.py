@@ -1,0 +1,419 @@
+#!/usr/bin/env python3
+"""Decode benchmark: Llama-3.1-8B architecture, batch 1, 2K context, B200.
+
+Metric: decode ms/token at bs=1 with a 2K context, plus the
+achieved HBM bandwidth against the measured peak. One "step" is one greedy
+decode token through the engine's public API (executor.begin -> runtime.run
+-> executor.finish) with all weights resident in HBM.
+
+Workload: seeded random-init BF16 weights (N(0,0.02), norms 1; no network
+for checkpoints), a 2048-token prefill of uniform random ids fills the KV
+cache, then W warm-up and K timed decode steps. The weights (16 GB) exceed
+L2 (126 MB), so no L2 flush is needed between steps.
+
+  value          device time per token (CUDA events, max over ranks)
+  e2e            the same step with the token id copied in from pinned host
+                 memory and the top-k read back every step
+  roofline       the dominant kernel (gate+up GEMV with SwiGLU), timed live
+  step_roofline  algorithmic bytes of the whole step / ms per token
+  cpu_baseline   the reference's algorithm (oracle restatement, torch CPU)
+                 on this host's cores, a bounded sample of decode steps
+
+--impl reference times that CPU path alone (rank 0) on the same config.
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "cascade-llm_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "decode ms/token, Llama-3.1-8B arch bs=1 (2K ctx)"
+LAYER_BYTES = 32 * 436_207_616
+HEAD_BYTES = 1_050_673_152
+NORM_BYTES = 532_480
+GATE_UP_BYTES = 234_881_024
+
+
+def step_bytes(context):
+    """Algorithmic HBM bytes of one decode token at `context` cached positions."""
+
+    return LAYER_BYTES + HEAD_BYTES + NORM_BYTES + 8192 + 131_072 * (context + 1) + 131_072
+
+
+def parse_args():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--context", type=int, default=2048)
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+    return args
+
+
+class Config:
+    hidden_size = 4096
+    intermediate_size = 14336
+    num_hidden_layers = 32
+    num_attention_heads = 32
+    num_key_value_heads = 8
+    vocab_size = 128256
+    rms_norm_eps = 1e-5
+    rope_parameters = {
+        "rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+        "original_max_position_embeddings": 8192, "rope_theta": 500000.0,
+    }
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as source:
+            return float(json.load(source)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL,
+            )
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(float(r[1]) for r in rows)
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for name, flag in zip(names, r[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {
+            "sm_mhz": sm[len(sm) // 2],
+            "sm_max_mhz": float(rows[0][2]),
+            "samples": len(rows),
+            "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "", 1).isdigit()) if rows else None,
+            "reasons": sorted(reasons),
+        }
+
+
+def random_ids(count, seed):
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randint(0, 128256, (1, count), generator=gen)
+
+
+def build_engine(device, context, extra):
+    import layer_streaming as ls
+
+    plan = ls.build_llama31_8b_plan("matrix_group")
+    store = ls.create_weight_store(plan, "full_pinned")
+    store.fill_seeded(seed=0, device=device)
+    resident = ls.ResidentDeviceArena(plan, store, device)
+    runtime = ls.DoubleBufferRuntime(plan, store, resident, device, weights="hbm")
+    executor = ls.Llama31DecodeExecutor(
+        Config(), resident, top_k=10, max_length=context + extra, allow_chunked_prefill=True
+    )
+    return plan, store, resident, runtime, executor
+
+
+def step(executor, runtime, ids):
+    state = executor.begin(ids)
+    state = runtime.run(executor, state)
+    return executor.finish(state)
+
+
+def prefill(executor, runtime, device, context, chunk=512):
+    ids = random_ids(context, seed=1).to(device)
+    state = None
+    with torch.inference_mode():
+        for start in range(0, context, chunk):
+            state = step(executor, runtime, ids[:, start:start + chunk])
+    torch.cuda.synchronize(device)
+    executor.check_errors()
+    return state.topk_indices[..., 0]
+
+
+def time_decode(executor, runtime, token, steps, warmup, barrier):
+    with torch.inference_mode():
+        for _ in range(warmup):
+            token = step(executor, runtime, token).topk_indices[..., 0]
+        torch.cuda.synchronize()
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            token = step(executor, runtime, token).topk_indices[..., 0]
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    return start.elapsed_time(end) / steps, token
+
+
+def time_e2e(executor, runtime, token, steps):
+    """Host-driven loop: id H2D from pinned memory, top-k D2H every step."""
+
+    ids_host = torch.empty((1, 1), dtype=torch.int64).pin_memory()
+    ids_host[0, 0] = int(token.reshape(-1)[0])
+    h2d = ids_host.numel() * ids_host.element_size()
+    d2h = 0
+    with torch.inference_mode():
+        torch.cuda.synchronize()
+        started = time.perf_counter()
+        for _ in range(steps):
+            state = step(executor, runtime, ids_host)
+            values = state.topk_values.cpu()
+            indices = state.topk_indices.cpu()
+            d2h = values.numel() * values.element_size() + indices.numel() * indices.element_size()
+            ids_host[0, 0] = int(indices.reshape(-1)[0])
+        elapsed = time.perf_counter() - started
+    return {"value": elapsed * 1000.0 / steps, "unit": "ms/token", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h}
+
+
+def time_gate_up(executor, runtime, plan, reps=4):
+    """Live timing of the dominant kernel: the 32 gate+up GEMVs back to back
+    (one per layer, so the 7.5 GB they read cannot come from L2)."""
+
+    from layer_streaming import ops
+
+    x = executor._x[0]
+    out = executor._mlp[0]
+    mats = []
+    for index, unit in enumerate(plan.units):
+        if unit.operation == "gate_up":
+            views = runtime.unit_views(index)
+            layer = unit.layer_index
+            mats.append((
+                views["model.layers.{}.mlp.gate_proj.weight".format(layer)],
+                views["model.layers.{}.mlp.up_proj.weight".format(layer)],
+                executor.resident["model.layers.{}.post_attention_layernorm.weight".format(layer)],
+            ))
+    stream = torch.cuda.current_stream()
+    for wg, wu, norm in mats:  # warm-up
+        ops.gate_up_swiglu(x, norm, 1e-5, wg, wu, out)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(reps):
+        for wg, wu, norm in mats:
+            ops.gate_up_swiglu(x, norm, 1e-5, wg, wu, out)
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / (reps * len(mats))
+
+
+def cpu_baseline(store, executor, context, budget_s):
+    """The reference's algorithm (oracle restatement, torch CPU) on the host."""
+
+    from oracle import llama_oracle as lo
+
+    weights = {key: store.tensor(key) for key in store.required_keys()}
+    oracle = lo.OracleDecoder(weights, top_k=10)
+    cache = executor.kv_cache
+    oracle.cache = [
+        (cache.key(i)[:, :context].unsqueeze(0).cpu(), cache.value(i)[:, :context].unsqueeze(0).cpu())
+        for i in range(32)
+    ]
+    oracle.length = context
+    token = torch.tensor([[1]])
+    times = []
+    with torch.inference_mode():
+        while sum(times) < budget_s and len(times) < 20:
+            started = time.perf_counter()
+            token = oracle.step(token)["indices"][..., 0]
+            times.append(time.perf_counter() - started)
+    steady = times[1:] if len(times) > 1 else times
+    return {
+        "value": 1000.0 * sum(steady) / len(steady),
+        "unit": "ms/token",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": "{} decode steps at a {}-token KV cache (engine's prefill copied to the host), "
+                  "first excluded; oracle/llama_oracle.py = the reference executor's torch ops".format(
+                      len(times), context),
+    }
+
+
+def reference_arm(args, rank):
+    """--impl reference: the reference's CPU algorithm on this host's cores."""
+
+    if rank != 0:
+        return None
+    from layer_streaming.plan import build_llama31_8b_plan
+    from oracle import llama_oracle as lo
+    from oracle.seeded import fill_model
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    plan = build_llama31_8b_plan("matrix_group")
+    weights = {k: torch.empty(s.shape, dtype=torch.bfloat16) for k, s in plan.tensors.items()}
+    fill_model(sorted(weights), weights.__getitem__, seed=0)
+    oracle = lo.OracleDecoder(weights, top_k=10)
+    gen = torch.Generator().manual_seed(2)
+    # a 2K context: random post-RoPE K/V stand in for a CPU prefill (~33 TFLOP)
+    oracle.cache = [
+        tuple((torch.randn((1, 8, args.context, 128), generator=gen)).to(torch.bfloat16) for _ in range(2))
+        for _ in range(32)
+    ]
+    oracle.length = args.context
+    token = torch.tensor([[1]])
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            token = oracle.step(token)["indices"][..., 0]
+        started = time.perf_counter()
+        for _ in range(args.steps):
+            token = oracle.step(token)["indices"][..., 0]
+        elapsed = time.perf_counter() - started
+    value = elapsed * 1000.0 / args.steps
+    sample = ("{} timed + {} warm-up decode steps at a {}-token context (random K/V cache); "
+              "oracle/llama_oracle.py restates the reference executor's torch ops").format(
+                  args.steps, args.warmup, args.context)
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": "ms/token", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, random token ids)",
+        "config": {"workload": "llama31-8b decode bs=1, {}-token context".format(args.context),
+                   "context": args.context, "flush": "weights (16 GB) larger than L2"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 3), "unit": "ms/token", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "ms/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = reference_arm(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        group = dist
+
+    def barrier():
+        if group is not None:
+            group.barrier()
+
+    extra = args.warmup + args.steps * 2 + 64
+    plan, store, resident, runtime, executor = build_engine(device, args.context, extra)
+    token = prefill(executor, runtime, device, args.context)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms, token = time_decode(executor, runtime, token, args.steps, args.warmup, barrier)
+    clock_info = clocks.stop()
+    executor.check_errors()
+    if group is not None:
+        t = torch.tensor([ms], device=device)
+        group.all_reduce(t, op=group.ReduceOp.MAX)
+        ms = float(t.item())
+    e2e = time_e2e(executor, runtime, token, args.steps)
+    gate_up_ms = time_gate_up(executor, runtime, plan)
+    peak, peak_kind = measured_peak()
+    context = executor.kv_cache.length - args.steps - 1  # mean cached length over the timed steps
+    achieved = GATE_UP_BYTES / (gate_up_ms / 1000.0) / 1e9
+    step_gbs = step_bytes(context) / (ms / 1000.0) / 1e9
+    baseline = None
+    if rank == 0 and not args.no_cpu_baseline:
+        baseline = cpu_baseline(store, executor, args.context, args.cpu_seconds)
+    kernels_per_step = 1 + 32 * 5 + 1 + 1  # embedding, 5 per layer, position advance, LM head
+    line = {
+        "metric": METRIC,
+        "value": round(ms, 4),
+        "unit": "ms/token",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, random token ids)",
+        "config": {
+            "workload": "llama31-8b decode bs=1, {}-token context".format(args.context),
+            "context": args.context,
+            "weights": "hbm-resident, matrix_group plan, resident vocab",
+            "flush": "none needed: weights (16 GB) larger than L2 (126 MB)",
+            "parallelism": "replicas" if world > 1 else "single GPU",
+        },
+        "tokens_per_s": round(1000.0 / ms * world, 2),
+        "e2e": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in e2e.items()},
+        "roofline": {
+            "bound": "hbm", "kernel": "gemv gate_up_swiglu (K=4096, N=2x14336)",
+            "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": None,
+            "ms_per_launch": round(gate_up_ms, 5), "bytes_per_launch": GATE_UP_BYTES,
+        },
+        "step_roofline": {
+            "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(step_gbs / peak, 4),
+            "frac_of_8tbs": round(step_gbs / 8000.0, 4), "bytes_per_token": step_bytes(context),
+        },
+        "cpu_baseline": baseline,
+        "gpu_launches": kernels_per_step * args.steps,
+        "clocks": clock_info,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if group is not None:
+        group.barrier()
+        group.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,148 @@
+// Shared device helpers for the sm_100a kernels of the decode engine.
+//
+// Everything here is hand-written PTX or plain CUDA: BF16 bit conversions,
+// mbarrier + cp.async.bulk (TMA bulk copy, global -> shared, no multicast)
+// wrappers, and programmatic-dependent-launch controls (griddepcontrol).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cb {
+
+// ---------------------------------------------------------------- bf16 bits
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ float bf16f(uint16_t h) { return __uint_as_float(uint32_t(h) << 16); }
+
+// Round-to-nearest-even fp32 -> bf16 (inputs are finite in this engine;
+// NaN is kept a NaN by forcing a mantissa bit).
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return uint16_t((u >> 16) | 0x40);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return uint16_t(u >> 16);
+}
+// fp32 value of the bf16 rounding of f (one torch bf16 op result).
+__device__ __forceinline__ float rbf(float f) { return bf16f(f2bf(f)); }
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.release.cta.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait: every spin in this engine gives up after `limit` polls,
+// records the failure in *err (if given) and returns false, so a lost
+// arrival can never hang the GPU. try_wait itself suspends for a
+// hardware-defined interval, so the bound is a wall-clock bound of roughly
+// limit x (suspend time); 1<<22 polls is well above a second.
+constexpr uint32_t kSpinLimit = 1u << 22;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (err) atomicExch(err, code);
+  return false;
+}
+
+// ------------------------------------------------- bulk copy (TMA, untiled)
+// Global -> shared::cta copy of `bytes` (multiple of 16, both addresses
+// 16-byte aligned) that completes `bytes` transactions on `bar`. No
+// multicast qualifier: every CTA fetches its own data.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Same, with an L2 eviction-priority hint: weights are streamed exactly once
+// per token, so they are marked evict_first to keep L2 for activations.
+__device__ __forceinline__ void bulk_g2s_stream(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                                uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, "
+      "[%3], %4;" ::"r"(smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ------------------------------------------ programmatic dependent launch
+// wait: block until every prerequisite grid has completed and its memory is
+// visible. launch: allow the dependent grid to be scheduled. Both are no-ops
+// for a kernel launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------------------ loads/stores
+// Activations written by an earlier kernel are read through L2 only (.cg):
+// with overlapping dependent launches no stale L1 line can be hit.
+__device__ __forceinline__ uint4 ld_cg_u4(const void* p) {
+  return __ldcg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+// Named barrier over `count` threads (multiple of 32) with id `id` (1..15).
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// dot of 8 bf16 weights with 8 bf16 activations, accumulated in fp32
+__device__ __forceinline__ float dot8(const uint4 w, const uint4 x, float acc) {
+  acc = fmaf(bf16lo(w.x), bf16lo(x.x), acc);
+  acc = fmaf(bf16hi(w.x), bf16hi(x.x), acc);
+  acc = fmaf(bf16lo(w.y), bf16lo(x.y), acc);
+  acc = fmaf(bf16hi(w.y), bf16hi(x.y), acc);
+  acc = fmaf(bf16lo(w.z), bf16lo(x.z), acc);
+  acc = fmaf(bf16hi(w.z), bf16hi(x.z), acc);
+  acc = fmaf(bf16lo(w.w), bf16lo(x.w), acc);
+  acc = fmaf(bf16hi(w.w), bf16hi(x.w), acc);
+  return acc;
+}
+
+}  // namespace cb

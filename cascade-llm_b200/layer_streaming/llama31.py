@@ -1,0 +1,418 @@
+"""Llama-3.1-8B decode executor on the sm_100a kernels.
+
+Drop-in for ``layer_streaming/llama31.py`` of the reference: the same class
+names, constructor signature, ``begin / __call__(unit, weights, state) /
+finish`` protocol and :class:`DecodeState` fields. Every tensor op of the
+reference is replaced by one fused kernel per transfer unit:
+
+==============  =====================================================  ============================
+unit            reference ops (llama31.py)                             kernel (torch.ops.cascade)
+==============  =====================================================  ============================
+qkv / q,k,v     RMSNorm :173-179, 3x F.linear :241-245, RoPE :206-212,  qkv_rope
+                KV-cache cat :44-50
+o_proj          repeat_kv + SDPA :182-234, F.linear + residual :246-250 attention, proj_residual
+gate_up / g,u   RMSNorm :255-263, F.linear, silu :264-271              gate_up_swiglu (gate_silu,
+                                                                       up_mul for ``matrix``)
+down_proj       gate*up, F.linear + residual :272-280                 proj_residual
+finish          RMSNorm :325-329, LM head + topk :330-348              lm_head_topk (+ vocab path)
+==============  =====================================================  ============================
+
+The KV cache is pre-allocated (:class:`StaticKVCache`, ``[layers, 2, 8,
+capacity, 128]``) and the request position is a device counter, so a
+one-token step has no host synchronisation and no allocation: with the
+weights resident in HBM (``DoubleBufferRuntime(weights="hbm")``) the whole
+layer stack of a decode step is captured once per context-length bucket and
+replayed as one CUDA graph.
+"""
+
+import math
+import os
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _native, ops
+
+LLAMA31_8B_MODEL_ID = "meta-llama/Llama-3.1-8B"
+MATRIX_ORDER = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+_UNIT_OPS = {
+    "layer": ("qkv", "o_proj", "gate_up", "down_proj"),
+    "qkv": ("qkv",),
+    "gate_up": ("gate_up",),
+}
+_TOPK_MAX = 64
+_DEFAULT_CAPACITY = 8192
+
+
+def _matrix_key(layer, name):
+    block = "self_attn" if name in ("q_proj", "k_proj", "v_proj", "o_proj") else "mlp"
+    return "model.layers.{}.{}.{}.weight".format(layer, block, name)
+
+
+def llama3_inv_freq(config):
+    """Inverse RoPE frequencies (fp32 [64]) for the config's rope parameters.
+
+    The llama3 frequency scaling of transformers'
+    ``_compute_llama3_parameters`` (modeling_rope_utils.py:550-626), which
+    the reference reaches through ``LlamaRotaryEmbedding`` (llama31.py:125),
+    evaluated once with the same fp32 operations.
+    """
+
+    params = dict(getattr(config, "rope_parameters", None) or {})
+    scaling = getattr(config, "rope_scaling", None) or {}
+    params = {**scaling, **params}
+    theta = float(params.get("rope_theta", getattr(config, "rope_theta", 500000.0)))
+    dim = config.hidden_size // config.num_attention_heads
+    exponents = torch.arange(0, dim, 2, dtype=torch.int64).to(dtype=torch.float)
+    inv_freq = 1.0 / (theta ** (exponents / dim))
+    rope_type = params.get("rope_type", params.get("type", "default"))
+    if rope_type == "default":
+        return inv_freq
+    if rope_type != "llama3":
+        raise ValueError("unsupported rope_type {!r} (llama3 or default)".format(rope_type))
+    factor = params["factor"]
+    low = params["low_freq_factor"]
+    high = params["high_freq_factor"]
+    old_len = params["original_max_position_embeddings"]
+    wavelen = 2 * math.pi / inv_freq
+    scaled = torch.where(wavelen > old_len / low, inv_freq / factor, inv_freq)
+    smooth = (old_len / wavelen - low) / (high - low)
+    smoothed = (1 - smooth) * scaled / factor + smooth * scaled
+    medium = ~(wavelen < old_len / high) * ~(wavelen > old_len / low)
+    return torch.where(medium, smoothed, scaled)
+
+
+def attention_split(tokens, length, sm_count):
+    """(splits, chunk) for the split-KV attention kernel: about two CTAs per
+    SM over (splits x 8 KV heads x tokens), chunks a multiple of 64 positions."""
+
+    target = max(1, (2 * sm_count) // (8 * tokens))
+    per_split = -(-length // target)
+    chunk = max(64, -(-per_split // 64) * 64)
+    return -(-length // chunk), chunk
+
+
+class StaticKVCache:
+    """Pre-allocated single-request KV cache ``[layers, 2, 8, capacity, 128]``.
+
+    Replaces ``SimpleKVCache`` (llama31.py:34-54), which re-allocates and
+    copies the whole cache with ``torch.cat`` on every token. Keys are stored
+    after RoPE, like the reference. ``position`` is the device int32 counter
+    of the next position; ``length`` is its host mirror. The storage is
+    allocated when an executor binds the cache to its device.
+    """
+
+    def __init__(self, layer_count=32, capacity=None, kv_heads=8, head_dim=128):
+        self.layer_count = int(layer_count)
+        self.capacity = int(capacity or os.environ.get("CASCADE_B200_MAX_LENGTH", _DEFAULT_CAPACITY))
+        self.kv_heads = kv_heads
+        self.head_dim = head_dim
+        self.storage = None
+        self.position = None
+        self.length = 0
+        self.generation = 0  # bumped when storage moves (invalidates graphs)
+
+    def bind(self, device):
+        if self.storage is None:
+            self._allocate(torch.device(device), self.capacity)
+        return self
+
+    def _allocate(self, device, capacity):
+        storage = torch.empty(
+            (self.layer_count, 2, self.kv_heads, capacity, self.head_dim), dtype=torch.bfloat16, device=device
+        )
+        if self.storage is not None and self.length:
+            storage[:, :, :, :self.length].copy_(self.storage[:, :, :, :self.length])
+        self.storage = storage
+        if self.position is None:
+            self.position = torch.zeros(1, dtype=torch.int32, device=device)
+        self.capacity = capacity
+        self.generation += 1
+
+    def reserve(self, length):
+        """Grow (copying the valid prefix) so that ``length`` positions fit."""
+
+        if length > self.capacity:
+            self._allocate(self.storage.device, max(length, 2 * self.capacity))
+
+    def key(self, layer):
+        return self.storage[layer, 0]
+
+    def value(self, layer):
+        return self.storage[layer, 1]
+
+    def sequence_length(self):
+        return self.length
+
+    @property
+    def entries(self):
+        """Per-layer ``(key, value)`` views ``[1, 8, length, 128]`` (None if empty)."""
+
+        if self.storage is None or self.length == 0:
+            return [None] * self.layer_count
+        return [
+            (self.storage[i, 0, :, :self.length].unsqueeze(0), self.storage[i, 1, :, :self.length].unsqueeze(0))
+            for i in range(self.layer_count)
+        ]
+
+    def clear(self):
+        self.length = 0
+        if self.position is not None:
+            ops.position_set(self.position, None, 0)
+
+
+SimpleKVCache = StaticKVCache
+
+
+@dataclass
+class DecodeState:
+    hidden_states: torch.Tensor
+    position_ids: torch.Tensor
+    layer_values: dict = field(default_factory=dict)
+    logits: object = None
+    topk_values: object = None
+    topk_indices: object = None
+
+
+class Llama31DecodeExecutor:
+    """Stateful callbacks consumed by :class:`DoubleBufferRuntime`.
+
+    One unpadded request: a multi-token prefill, then one-token decode steps
+    (``allow_chunked_prefill=True`` additionally accepts multi-token steps
+    after the prefill, which the reference refuses). ``max_length`` sizes the
+    KV cache (grown on demand). ``use_graphs`` enables CUDA-graph replay of
+    one-token steps when the runtime keeps the weights in HBM.
+    """
+
+    def __init__(self, config, resident, kv_cache=None, vocab_runtime=None, top_k=10,
+                 return_full_logits=False, max_length=None, allow_chunked_prefill=False,
+                 use_graphs=True):
+        expected = {
+            "hidden_size": 4096,
+            "intermediate_size": 14336,
+            "num_hidden_layers": 32,
+            "num_attention_heads": 32,
+            "num_key_value_heads": 8,
+            "vocab_size": 128256,
+        }
+        for name, value in expected.items():
+            if getattr(config, name, None) != value:
+                raise ValueError(
+                    "config {}={} is not Llama-3.1-8B value {}".format(name, getattr(config, name, None), value)
+                )
+        self.config = config
+        self.resident = resident
+        self.vocab_runtime = vocab_runtime
+        self.top_k = int(top_k)
+        self.return_full_logits = bool(return_full_logits)
+        if self.top_k < 1:
+            raise ValueError("top_k must be positive")
+        if self.top_k > _TOPK_MAX:
+            raise ValueError("the fused LM-head kernel supports top_k <= {}".format(_TOPK_MAX))
+        self.device = torch.device(resident.device)
+        if self.device.type != "cuda":
+            raise RuntimeError("the B200 executor needs a CUDA device (there is no CPU path)")
+        self.eps = float(getattr(config, "rms_norm_eps", 1e-5))
+        self.allow_chunked_prefill = bool(allow_chunked_prefill)
+        self.use_graphs = bool(use_graphs) and os.environ.get("CASCADE_B200_GRAPHS", "1") != "0"
+        lib = _native.lib()
+        with torch.cuda.device(self.device):
+            _native.check(lib.cb_prepare(), "cb_prepare")
+            self.kv_cache = kv_cache if kv_cache is not None else StaticKVCache(config.num_hidden_layers)
+            if not isinstance(self.kv_cache, StaticKVCache):
+                raise TypeError("kv_cache must be a StaticKVCache (SimpleKVCache)")
+            if max_length is not None:
+                self.kv_cache.capacity = max(self.kv_cache.capacity, int(max_length))
+            self.kv_cache.bind(self.device)
+            self.inv_freq = llama3_inv_freq(config).to(self.device)
+            self.error_word = torch.zeros(1, dtype=torch.int32, device=self.device)
+            _native.check(lib.cb_set_error_word(self.error_word.data_ptr()), "cb_set_error_word")
+            self.lm_workspace = torch.empty(
+                ops.lm_head_workspace_bytes(self.top_k), dtype=torch.uint8, device=self.device
+            )
+            self.lm_ticket = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.sm_count = int(lib.cb_sm_count())
+        self._graphs = {}
+        self._rows = 0
+        self._buffers(1)
+        self._attn_ws = None
+        self._attn_ws_bytes = 0
+        self._tokens = 0
+
+    # ---------------------------------------------------------------- buffers
+    def _buffers(self, rows):
+        """Activation rows: residual stream x, q, attention output, mlp."""
+
+        if rows <= self._rows:
+            return
+        rows = max(rows, 2 * self._rows)
+        dev = self.device
+        self._x = torch.empty((rows, 4096), dtype=torch.bfloat16, device=dev)
+        self._q = torch.empty((rows, 4096), dtype=torch.bfloat16, device=dev)
+        self._attn = torch.empty((rows, 4096), dtype=torch.bfloat16, device=dev)
+        self._mlp = torch.empty((rows, 14336), dtype=torch.bfloat16, device=dev)
+        self._tickets = torch.zeros(8 * rows, dtype=torch.int32, device=dev)  # kept zero by the kernel
+        self._rows = rows
+        self._graphs.clear()
+
+    def attention_config(self, tokens, length):
+        return attention_split(tokens, length, self.sm_count)
+
+    def _attention_workspace(self, tokens, splits):
+        need = ops.attention_workspace_bytes(tokens, splits)
+        if need > self._attn_ws_bytes:
+            self._attn_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            self._attn_ws_bytes = need
+            self._graphs.clear()
+        return self._attn_ws
+
+    def check_errors(self):
+        """Raise if a kernel reported a timed-out wait or a bad index."""
+
+        code = int(self.error_word.item())
+        if code:
+            self.error_word.zero_()
+            raise RuntimeError("a cascade kernel reported device error code {}".format(code))
+
+    # ---------------------------------------------------------------- protocol
+    def begin(self, input_ids, position_ids=None):
+        if input_ids.ndim != 2 or input_ids.shape[0] != 1:
+            raise ValueError("first runtime supports one unpadded request")
+        past = self.kv_cache.sequence_length()
+        tokens = int(input_ids.shape[1])
+        if tokens < 1:
+            raise ValueError("input_ids is empty")
+        if past and tokens != 1 and not self.allow_chunked_prefill:
+            raise ValueError("after prefill, only one-token decode calls are supported")
+        with torch.cuda.device(self.device):
+            if position_ids is not None:
+                start = int(position_ids.reshape(-1)[0])
+                if start != past:
+                    raise ValueError("position_ids must continue the cached sequence ({} != {})".format(start, past))
+            self.kv_cache.reserve(past + tokens)
+            self._buffers(tokens)
+            ids = input_ids.reshape(-1)
+            if ids.device != self.device or ids.dtype != torch.int64 or not ids.is_contiguous():
+                ids = ids.to(device=self.device, dtype=torch.int64).contiguous()
+            if self.vocab_runtime is None:
+                ops.embedding(ids, self.resident["model.embed_tokens.weight"], self._x[:tokens])
+            else:
+                self._x[:tokens].copy_(self.vocab_runtime.embedding(ids.view(1, -1)).view(tokens, -1))
+        self._tokens = tokens
+        return DecodeState(
+            hidden_states=self._x[:tokens].view(1, tokens, 4096),
+            position_ids=torch.arange(past, past + tokens, dtype=torch.long).unsqueeze(0),
+        )
+
+    def _unit(self, layer, operation, weights, splits=None, chunk=None):
+        tokens = self._tokens
+        cache = self.kv_cache
+        eps = self.eps
+        pos = cache.position
+        res = self.resident
+        norm_in = res["model.layers.{}.input_layernorm.weight".format(layer)]
+        norm_post = res["model.layers.{}.post_attention_layernorm.weight".format(layer)]
+        w = lambda name: weights[_matrix_key(layer, name)]
+        kc, vc = cache.key(layer), cache.value(layer)
+        if operation in ("qkv", "q_proj", "k_proj", "v_proj"):
+            wq = w("q_proj") if operation in ("qkv", "q_proj") else None
+            wk = w("k_proj") if operation in ("qkv", "k_proj") else None
+            wv = w("v_proj") if operation in ("qkv", "v_proj") else None
+            for m in range(tokens):
+                ops.qkv_rope(
+                    self._x[m], norm_in, eps, wq, wk, wv, self.inv_freq, pos, m,
+                    self._q[m] if wq is not None else None,
+                    kc if wk is not None else None, vc if wv is not None else None,
+                )
+        elif operation == "o_proj":
+            if splits is None:
+                splits, chunk = self.attention_config(tokens, cache.length + tokens)
+            ws = self._attention_workspace(tokens, splits)
+            ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
+            wo = w("o_proj")
+            for m in range(tokens):
+                ops.proj_residual(self._attn[m], wo, self._x[m], self._x[m])
+        elif operation == "gate_up":
+            wg, wu = w("gate_proj"), w("up_proj")
+            for m in range(tokens):
+                ops.gate_up_swiglu(self._x[m], norm_post, eps, wg, wu, self._mlp[m])
+        elif operation == "gate_proj":
+            for m in range(tokens):
+                ops.gate_silu(self._x[m], norm_post, eps, w("gate_proj"), self._mlp[m])
+        elif operation == "up_proj":
+            for m in range(tokens):
+                ops.up_mul(self._x[m], norm_post, eps, w("up_proj"), self._mlp[m])
+        elif operation == "down_proj":
+            wd = w("down_proj")
+            for m in range(tokens):
+                ops.proj_residual(self._mlp[m], wd, self._x[m], self._x[m])
+        else:
+            raise ValueError("unknown Llama operation {}".format(operation))
+
+    def _after_last_unit(self):
+        # the step's K/V are cached: advance the device position counter
+        ops.position_advance(self.kv_cache.position, self._tokens)
+        self.kv_cache.length += self._tokens
+
+    def __call__(self, unit, weights, state):
+        for operation in _UNIT_OPS.get(unit.operation, (unit.operation,)):
+            self._unit(unit.layer_index, operation, weights)
+        if unit.layer_index == self.config.num_hidden_layers - 1 and unit.operation in ("layer", "down_proj"):
+            self._after_last_unit()
+        return state
+
+    def run_units_resident(self, runtime, state):
+        """All units of a step with HBM-resident weights (graph replay for M=1)."""
+
+        units = runtime.plan.units
+        if not self.use_graphs or self._tokens != 1:
+            for index, unit in enumerate(units):
+                state = self(unit, runtime.unit_views(index), state)
+            return state
+        length = self.kv_cache.length + 1
+        bucket = max(64, 1 << (length - 1).bit_length())
+        bucket = min(bucket, self.kv_cache.capacity)
+        splits, chunk = self.attention_config(1, bucket)
+        key = (id(runtime), bucket, self.kv_cache.generation, self._rows)
+        graph = self._graphs.get(key)
+        if graph is None:
+            self._attention_workspace(1, splits)
+            graph = torch.cuda.CUDAGraph()
+            saved = self.kv_cache.length
+            with torch.cuda.graph(graph):
+                for index, unit in enumerate(units):
+                    for operation in _UNIT_OPS.get(unit.operation, (unit.operation,)):
+                        self._unit(unit.layer_index, operation, runtime.unit_views(index), splits, chunk)
+                ops.position_advance(self.kv_cache.position, 1)
+            self.kv_cache.length = saved
+            key = (id(runtime), bucket, self.kv_cache.generation, self._rows)
+            self._graphs[key] = graph
+        graph.replay()
+        self.kv_cache.length += 1
+        return state
+
+    def finish(self, state):
+        tokens = self._tokens
+        last = self._x[tokens - 1]
+        k = min(self.top_k, self.config.vocab_size)
+        with torch.cuda.device(self.device):
+            if self.vocab_runtime is None:
+                values = torch.empty((1, 1, k), dtype=torch.float32, device=self.device)
+                indices = torch.empty((1, 1, k), dtype=torch.int64, device=self.device)
+                logits = None
+                if self.return_full_logits:
+                    logits = torch.empty((1, 1, self.config.vocab_size), dtype=torch.float32, device=self.device)
+                ops.lm_head_topk(
+                    last, self.resident["model.norm.weight"], self.eps, self.resident["lm_head.weight"], 0, k,
+                    None if logits is None else logits.view(-1), values.view(-1), indices.view(-1),
+                    self.lm_workspace, self.lm_ticket,
+                )
+            else:
+                normed = torch.empty((1, 1, 4096), dtype=torch.bfloat16, device=self.device)
+                ops.rmsnorm(last, self.resident["model.norm.weight"], self.eps, normed.view(-1))
+                result = self.vocab_runtime.lm_head_topk(normed, top_k=k, return_full_logits=self.return_full_logits)
+                values, indices, logits = result["values"], result["indices"], result["logits"]
+        state.topk_values = values
+        state.topk_indices = indices
+        state.logits = logits
+        return state

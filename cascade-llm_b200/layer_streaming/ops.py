@@ -1,0 +1,238 @@
+"""Torch operators ``torch.ops.cascade.*`` over the C ABI of libcascade_b200.
+
+Each operator validates its tensors and launches one hand-written sm_100a
+kernel on the current CUDA stream (no host synchronisation, so every
+operator can be captured into a CUDA graph). Operators only have a CUDA
+implementation: called with CPU tensors they raise, there is no fallback.
+Reference op each one replaces is cited in ``include/cascade_b200.h``.
+"""
+
+import torch
+
+from . import _native as nat
+
+BF16 = torch.bfloat16
+_LIB = torch.library.Library("cascade", "DEF")
+
+_SCHEMAS = {
+    "embedding": "embedding(Tensor ids, Tensor table, Tensor(a!) out) -> ()",
+    "rmsnorm": "rmsnorm(Tensor x, Tensor weight, float eps, Tensor(a!) out) -> ()",
+    "qkv_rope": (
+        "qkv_rope(Tensor x, Tensor? norm_w, float eps, Tensor? wq, Tensor? wk, Tensor? wv, "
+        "Tensor inv_freq, Tensor position, int token, Tensor(a!)? q_out, Tensor(b!)? k_cache, "
+        "Tensor(c!)? v_cache) -> ()"
+    ),
+    "proj_residual": "proj_residual(Tensor x, Tensor w, Tensor residual, Tensor(a!) out) -> ()",
+    "gate_up_swiglu": (
+        "gate_up_swiglu(Tensor x, Tensor? norm_w, float eps, Tensor w_gate, Tensor w_up, "
+        "Tensor(a!) out) -> ()"
+    ),
+    "gate_silu": "gate_silu(Tensor x, Tensor? norm_w, float eps, Tensor w_gate, Tensor(a!) out) -> ()",
+    "up_mul": "up_mul(Tensor x, Tensor? norm_w, float eps, Tensor w_up, Tensor(a!) gate_act) -> ()",
+    "lm_head_topk": (
+        "lm_head_topk(Tensor x, Tensor? norm_w, float eps, Tensor w, int row_offset, int k, "
+        "Tensor(a!)? logits, Tensor(b!) out_values, Tensor(c!) out_indices, Tensor(d!) workspace, "
+        "Tensor(e!) ticket) -> ()"
+    ),
+    "topk_merge": (
+        "topk_merge(Tensor? a_values, Tensor? a_indices, Tensor b_values, Tensor b_indices, int k, "
+        "Tensor(a!) out_values, Tensor(b!) out_indices) -> ()"
+    ),
+    "attention": (
+        "attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor position, int splits, int chunk, "
+        "Tensor(a!) out, Tensor(b!) workspace, Tensor(c!) tickets) -> ()"
+    ),
+    "position_set": "position_set(Tensor(a!) position, Tensor? src, int value) -> ()",
+    "position_advance": "position_advance(Tensor(a!) position, int count) -> ()",
+}
+
+
+def _stream(t):
+    return nat.stream_ptr(t.device)
+
+
+def embedding(ids, table, out):
+    m = ids.numel()
+    nat.check(
+        nat.lib().cb_embedding(
+            nat.ptr(ids, torch.int64, "ids"), m, nat.ptr(table, BF16, "table"),
+            table.shape[0], table.shape[1], nat.ptr(out, BF16, "out"), _stream(out),
+        ),
+        "cascade.embedding",
+    )
+
+
+def rmsnorm(x, weight, eps, out):
+    hidden = x.shape[-1]
+    nat.check(
+        nat.lib().cb_rmsnorm(
+            nat.ptr(x, BF16, "x"), nat.ptr(weight, BF16, "weight"), x.numel() // hidden, hidden,
+            float(eps), nat.ptr(out, BF16, "out"), _stream(out),
+        ),
+        "cascade.rmsnorm",
+    )
+
+
+def qkv_rope(x, norm_w, eps, wq, wk, wv, inv_freq, position, token, q_out, k_cache, v_cache):
+    cache = k_cache if k_cache is not None else v_cache
+    cache_len = cache.shape[-2] if cache is not None else 0
+    nat.check(
+        nat.lib().cb_qkv_rope(
+            nat.ptr(x, BF16, "x"), nat.ptr(norm_w, BF16, "norm_w"), float(eps),
+            nat.ptr(wq, BF16, "wq"), nat.ptr(wk, BF16, "wk"), nat.ptr(wv, BF16, "wv"),
+            nat.ptr(inv_freq, torch.float32, "inv_freq"), nat.ptr(position, torch.int32, "position"),
+            int(token), nat.ptr(q_out, BF16, "q_out"), nat.ptr(k_cache, BF16, "k_cache"),
+            nat.ptr(v_cache, BF16, "v_cache"), cache_len, _stream(x),
+        ),
+        "cascade.qkv_rope",
+    )
+
+
+def proj_residual(x, w, residual, out):
+    nat.check(
+        nat.lib().cb_proj_residual(
+            nat.ptr(x, BF16, "x"), w.shape[1], nat.ptr(w, BF16, "w"), w.shape[0],
+            nat.ptr(residual, BF16, "residual"), nat.ptr(out, BF16, "out"), _stream(x),
+        ),
+        "cascade.proj_residual",
+    )
+
+
+def gate_up_swiglu(x, norm_w, eps, w_gate, w_up, out):
+    nat.check(
+        nat.lib().cb_gate_up_swiglu(
+            nat.ptr(x, BF16, "x"), nat.ptr(norm_w, BF16, "norm_w"), float(eps),
+            nat.ptr(w_gate, BF16, "w_gate"), nat.ptr(w_up, BF16, "w_up"),
+            nat.ptr(out, BF16, "out"), _stream(x),
+        ),
+        "cascade.gate_up_swiglu",
+    )
+
+
+def gate_silu(x, norm_w, eps, w_gate, out):
+    nat.check(
+        nat.lib().cb_gate_silu(
+            nat.ptr(x, BF16, "x"), nat.ptr(norm_w, BF16, "norm_w"), float(eps),
+            nat.ptr(w_gate, BF16, "w_gate"), nat.ptr(out, BF16, "out"), _stream(x),
+        ),
+        "cascade.gate_silu",
+    )
+
+
+def up_mul(x, norm_w, eps, w_up, gate_act):
+    nat.check(
+        nat.lib().cb_up_mul(
+            nat.ptr(x, BF16, "x"), nat.ptr(norm_w, BF16, "norm_w"), float(eps),
+            nat.ptr(w_up, BF16, "w_up"), nat.ptr(gate_act, BF16, "gate_act"), _stream(x),
+        ),
+        "cascade.up_mul",
+    )
+
+
+def lm_head_workspace_bytes(k):
+    return int(nat.lib().cb_lm_head_workspace_bytes(int(k)))
+
+
+def lm_head_topk(x, norm_w, eps, w, row_offset, k, logits, out_values, out_indices, workspace, ticket):
+    nat.check(
+        nat.lib().cb_lm_head_topk(
+            nat.ptr(x, BF16, "x"), nat.ptr(norm_w, BF16, "norm_w"), float(eps),
+            nat.ptr(w, BF16, "w"), w.shape[0], int(row_offset), int(k),
+            nat.ptr(logits, torch.float32, "logits"), nat.ptr(out_values, torch.float32, "out_values"),
+            nat.ptr(out_indices, torch.int64, "out_indices"), nat.ptr(workspace, None, "workspace"),
+            nat.ptr(ticket, torch.int32, "ticket"), _stream(x),
+        ),
+        "cascade.lm_head_topk",
+    )
+
+
+def topk_merge(a_values, a_indices, b_values, b_indices, k, out_values, out_indices):
+    na = 0 if a_values is None else a_values.numel()
+    nat.check(
+        nat.lib().cb_topk_merge(
+            nat.ptr(a_values, torch.float32, "a_values"), nat.ptr(a_indices, torch.int64, "a_indices"),
+            na, nat.ptr(b_values, torch.float32, "b_values"),
+            nat.ptr(b_indices, torch.int64, "b_indices"), b_values.numel(), int(k),
+            nat.ptr(out_values, torch.float32, "out_values"),
+            nat.ptr(out_indices, torch.int64, "out_indices"), _stream(b_values),
+        ),
+        "cascade.topk_merge",
+    )
+
+
+def attention_workspace_bytes(m, splits):
+    return int(nat.lib().cb_attention_workspace_bytes(int(m), int(splits)))
+
+
+def attention(q, k_cache, v_cache, position, splits, chunk, out, workspace, tickets):
+    m = q.numel() // 4096
+    if tickets.numel() < 8 * m:
+        raise ValueError("attention needs 8 tickets per token")
+    nat.check(
+        nat.lib().cb_attention(
+            nat.ptr(q, BF16, "q"), nat.ptr(k_cache, BF16, "k_cache"), nat.ptr(v_cache, BF16, "v_cache"),
+            k_cache.shape[-2], nat.ptr(position, torch.int32, "position"), m, int(splits), int(chunk),
+            nat.ptr(out, BF16, "out"), nat.ptr(workspace, None, "workspace"),
+            nat.ptr(tickets, torch.int32, "tickets"), _stream(q),
+        ),
+        "cascade.attention",
+    )
+
+
+def position_set(position, src, value):
+    nat.check(
+        nat.lib().cb_position_set(
+            nat.ptr(position, torch.int32, "position"), nat.ptr(src, torch.int64, "src"),
+            int(value), _stream(position),
+        ),
+        "cascade.position_set",
+    )
+
+
+def position_advance(position, count):
+    nat.check(
+        nat.lib().cb_position_advance(
+            nat.ptr(position, torch.int32, "position"), int(count), _stream(position)
+        ),
+        "cascade.position_advance",
+    )
+
+
+def fill_normal_(tensor, key, std=0.02, offset=0):
+    nat.check(
+        nat.lib().cb_fill_normal_bf16(
+            nat.ptr(tensor, BF16, "tensor"), tensor.numel(), int(offset), int(key), float(std),
+            _stream(tensor),
+        ),
+        "cascade.fill_normal_",
+    )
+    return tensor
+
+
+def fill_(tensor, value):
+    nat.check(
+        nat.lib().cb_fill_bf16(nat.ptr(tensor, BF16, "tensor"), tensor.numel(), float(value), _stream(tensor)),
+        "cascade.fill_",
+    )
+    return tensor
+
+
+def memcpy_h2d_async(dst, src):
+    """cudaMemcpyAsync of a host tensor into a device tensor (same bytes)."""
+
+    nbytes = src.numel() * src.element_size()
+    if dst.numel() * dst.element_size() < nbytes:
+        raise ValueError("destination is smaller than the source")
+    if src.device.type != "cpu" or dst.device.type != "cuda":
+        raise ValueError("memcpy_h2d_async copies host -> device")
+    if not (src.is_contiguous() and dst.is_contiguous()):
+        raise ValueError("memcpy_h2d_async needs contiguous tensors")
+    nat.check(
+        nat.lib().cb_memcpy_h2d_async(dst.data_ptr(), src.data_ptr(), nbytes, _stream(dst)),
+        "cascade.memcpy_h2d_async",
+    )
+
+
+for _name, _schema in _SCHEMAS.items():
+    _LIB.define(_schema)
+    _LIB.impl(_name, globals()[_name], "CUDA")

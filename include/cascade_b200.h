@@ -1,0 +1,162 @@
+/*
+ * cascade_b200.h - C ABI of libcascade_b200.so, the sm_100a kernels behind the
+ * Llama-3.1-8B decode path of Cascade-LLM's `layer_streaming` package.
+ *
+ * Conventions for every entry point:
+ *   - plain device pointers (BF16 data as `void*`, row-major, 16-byte aligned),
+ *     element counts, and a `cudaStream_t` passed as `void* stream`;
+ *   - nothing allocates: scratch workspaces and zero-initialised counters
+ *     are caller-provided (the kernels leave the counters zero again);
+ *   - the return value is 0 on success, else a nonzero cb_status code, and
+ *     cb_last_error() describes the failure (thread-local);
+ *   - kernels are enqueued asynchronously on `stream`; none synchronises the
+ *     host, so calls can be captured into a CUDA graph;
+ *   - each BF16 rounding point of the reference's PyTorch ops is reproduced
+ *     (llama31.py: F.linear -> bf16, residual adds, SiLU, gate*up, RoPE).
+ *
+ * Reference file:line citations are paths inside the Cascade-LLM project.
+ */
+#ifndef CASCADE_B200_H
+#define CASCADE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum cb_status { CB_OK = 0, CB_ERR_INVALID = 1, CB_ERR_CUDA = 2, CB_ERR_UNSUPPORTED = 3 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int cb_version(void);
+/* Message of the last failure on this host thread ("" if none). */
+const char* cb_last_error(void);
+/* Enable (1) / disable (0) programmatic dependent launch between the
+ * engine's kernels (default: enabled). Returns the previous setting. */
+int cb_set_pdl(int enable);
+/* Number of SMs of the current device (grid size of the streaming kernels). */
+int cb_sm_count(void);
+/* One-time per-device set-up of the kernels (shared-memory limits). Call it
+ * with the device current before capturing engine calls into a CUDA graph;
+ * entry points otherwise do it on first use. */
+int cb_prepare(void);
+/* Registers a caller-owned device int32 (zeroed) that kernels set to a
+ * nonzero code when a bounded wait gives up or an index is out of range,
+ * instead of hanging or faulting. NULL disables the reporting. One word per
+ * process (one process per GPU). The host reads it between steps. */
+int cb_set_error_word(int32_t* device_word);
+
+/* ---------------------------------------------------------------- set-up */
+
+/* Seeded N(0, std) BF16 initialiser: element i of the stream `key`
+ * (key = cb_stream_key(seed, tensor_name)). Same bits as the CPU oracle.
+ * Replaces the checkpoint load of layer_streaming/weight_store.py:109-171
+ * for the random-init benchmark configurations. */
+uint64_t cb_stream_key(uint64_t seed, const char* tensor_name);
+int cb_fill_normal_bf16(void* out, int64_t n, int64_t offset, uint64_t key, double std_dev,
+                        void* stream);
+int cb_fill_bf16(void* out, int64_t n, float value, void* stream);
+
+/* Device position counter of the request (int32): the first position of
+ * the next step. cb_position_set copies an int64 device position (e.g.
+ * position_ids[0, 0]) or, if src is NULL, `value`. cb_position_advance adds
+ * `count` (after a step of `count` tokens). */
+int cb_position_set(int32_t* position, const int64_t* src, int32_t value, void* stream);
+int cb_position_advance(int32_t* position, int32_t count, void* stream);
+
+/* ---------------------------------------------------------------- layers */
+
+/* Row gather of token embeddings. Replaces F.embedding
+ * (layer_streaming/llama31.py:144-148). ids: int64 [M] (device);
+ * table: [vocab, hidden]; out: [M, hidden]. Out-of-range ids -> error word. */
+int cb_embedding(const int64_t* ids, int M, const void* table, int64_t vocab, int hidden, void* out,
+                 void* stream);
+
+/* RMSNorm (layer_streaming/llama31.py:21-25): out = bf16(w * bf16(x * rsqrt(mean(x^2)+eps))).
+ * x, out: [M, hidden]; w: [hidden]. */
+int cb_rmsnorm(const void* x, const void* w, int M, int hidden, float eps, void* out, void* stream);
+
+/* Fused input RMSNorm + Q/K/V projection + RoPE + KV-cache write for token
+ * `token` of the step (position = *position + token). Replaces
+ * llama31.py:173-179 (_start_attention), :238-245 (q/k/v F.linear) and the
+ * RoPE + SimpleKVCache.append of :200-217. Any of wq/wk/wv may be NULL (the
+ * `matrix` granularity streams them as separate units); present ones need
+ * their output. x: hidden row [4096] of this token; norm_w: [4096] or NULL
+ * (x already normalised); wq [4096,4096], wk/wv [1024,4096]; inv_freq: fp32
+ * [64] (llama3-scaled); q_out: [4096] (this token's row); k_cache/v_cache:
+ * this layer's [8, cache_len, 128]. */
+int cb_qkv_rope(const void* x, const void* norm_w, float eps, const void* wq, const void* wk,
+                const void* wv, const float* inv_freq, const int32_t* position, int token,
+                void* q_out, void* k_cache, void* v_cache, int64_t cache_len, void* stream);
+
+/* out = bf16(residual + bf16(x . W^T)) for one token row. Replaces the o_proj
+ * (llama31.py:246-250) and down_proj (:272-280) F.linear + residual add.
+ * K in {4096, 14336}; W: [N, K]; x: [K]; residual/out: [N] (may alias). */
+int cb_proj_residual(const void* x, int K, const void* w, int N, const void* residual, void* out,
+                     void* stream);
+
+/* Post-attention RMSNorm + gate/up projection + SwiGLU for one token row:
+ * out = bf16(bf16(silu(bf16(xn . Wg^T))) * bf16(xn . Wu^T)). Replaces
+ * llama31.py:252-275 (the matrix_group `gate_up` unit). W_gate/W_up:
+ * [14336, 4096]; out: [14336]. */
+int cb_gate_up_swiglu(const void* x, const void* norm_w, float eps, const void* w_gate,
+                      const void* w_up, void* out, void* stream);
+/* The same split in two for the `matrix` granularity (gate_proj and up_proj
+ * are separate units, llama31.py:252-271): cb_gate_silu writes
+ * bf16(silu(...)), cb_up_mul multiplies it by the up projection in place. */
+int cb_gate_silu(const void* x, const void* norm_w, float eps, const void* w_gate, void* out,
+                 void* stream);
+int cb_up_mul(const void* x, const void* norm_w, float eps, const void* w_up, void* gate_act,
+              void* stream);
+
+/* Fused final RMSNorm + LM-head logits + exact top-k over `rows` vocabulary
+ * rows (a 16,384-row chunk, a vocab shard, or the whole head). Replaces
+ * llama31.py:325-339 and the per-chunk F.linear/.float()/topk of
+ * layer_streaming/vocab.py:247-253. Logits are bf16-rounded then fp32, as
+ * F.linear(...).float(). Indices are row_offset + row. Order: larger value
+ * first, then smaller index. k <= 64 and k <= rows. logits (fp32 [rows]) may
+ * be NULL. workspace: cb_lm_head_workspace_bytes(k) bytes of scratch (no
+ * initialisation). ticket: one uint32, zeroed once by the caller, used by
+ * the last CTA to finish the merge and reset to zero by it. */
+int64_t cb_lm_head_workspace_bytes(int k);
+int cb_lm_head_topk(const void* x, const void* norm_w, float eps, const void* w, int64_t rows,
+                    int64_t row_offset, int k, float* logits, float* out_values,
+                    int64_t* out_indices, void* workspace, unsigned int* ticket, void* stream);
+
+/* Exact merge of two candidate sets (values fp32, indices int64) into the
+ * top k (k <= 64). Replaces merge_topk (layer_streaming/vocab.py:11-32); also
+ * merges the all-gathered per-rank candidates of a vocab-sharded head.
+ * `a` may be NULL with na = 0. Output may alias neither input. */
+int cb_topk_merge(const float* a_values, const int64_t* a_indices, int na, const float* b_values,
+                  const int64_t* b_indices, int nb, int k, float* out_values, int64_t* out_indices,
+                  void* stream);
+
+/* GQA attention of M query tokens at positions *position .. *position+M-1
+ * over the cache [0, *position + M) (causal within the step). Replaces
+ * llama31.py:182-234 (_repeat_kv + scaled_dot_product_attention): scale
+ * 1/sqrt(128), fp32 softmax, bf16 output [M, 4096]. Split-KV: `splits`
+ * chunks per (token, kv head), combined by the last CTA of each group.
+ * q: [M, 32, 128]; k_cache/v_cache: this layer's [8, cache_len, 128].
+ * chunk = positions per split (multiple of 64); splits*chunk must cover the
+ * longest context of the step. workspace: cb_attention_workspace_bytes(M,
+ * splits) bytes of scratch for the per-split partials (no initialisation).
+ * tickets: M*8 uint32 counters, zeroed once by the caller; each launch
+ * leaves them zero. */
+int64_t cb_attention_workspace_bytes(int M, int splits);
+int cb_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
+                 const int32_t* position, int M, int splits, int chunk, void* out, void* workspace,
+                 unsigned int* tickets, void* stream);
+
+/* ---------------------------------------------------------------- copies */
+
+/* Host -> device copy of `bytes` on `stream` (cudaMemcpyAsync). The H2D leg
+ * of DoubleBufferRuntime.run (layer_streaming/runtime.py:194-204) and of the
+ * vocab chunks (layer_streaming/vocab.py:228-236). `src` must be pinned for
+ * the copy to be asynchronous. */
+int cb_memcpy_h2d_async(void* dst, const void* src, int64_t bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CASCADE_B200_H */

@@ -1,0 +1,280 @@
+"""Model-level parity on the GPU.
+
+Seeded random-init Llama-3.1-8B, the 6-token seeded prompt, prefill + 8
+greedy decode steps, top-k 10, driven exactly like tools/run_llama31.py
+(plan -> store -> ResidentDeviceArena -> DoubleBufferRuntime [->
+VocabStreamingRuntime] -> executor.begin/run/finish). Checked against
+  * the golden run of the reference's own code (tests/golden/config0.*),
+  * the oracle's restatement running with torch ops on the same GPU and the
+    same device weights (the reference's PyTorch GPU path),
+with the north-star criteria: top-k values within rtol 2e-2 / atol 2e-2 and
+ids identical wherever the neighbouring gaps exceed that tolerance, greedy
+ids identical over the 8 decode steps. Full logits: after 32 random-init
+layers the reference's own GPU and CPU runs differ by up to ~0.3 (mean
+~0.05), so the engine is held to that noise floor (cosine, max-abs, RMSE)
+rather than to a per-element 2e-2 that the reference fails against itself;
+the per-element tolerance is checked per layer (kernel tests, smoke).
+"""
+
+import json
+
+import pytest
+import torch
+from safetensors.torch import load_file
+
+from conftest import golden_path
+from oracle import llama_oracle as lo
+from oracle.seeded import prompt_ids
+
+pytestmark = pytest.mark.gpu
+
+RTOL = ATOL = 2e-2
+
+
+class Config:
+    hidden_size = 4096
+    intermediate_size = 14336
+    num_hidden_layers = 32
+    num_attention_heads = 32
+    num_key_value_heads = 8
+    vocab_size = 128256
+    rms_norm_eps = 1e-5
+    rope_parameters = {
+        "rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+        "original_max_position_embeddings": 8192, "rope_theta": 500000.0,
+    }
+
+
+@pytest.fixture(scope="module")
+def meta():
+    return json.load(open(golden_path("config0.json")))
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return load_file(golden_path("config0.safetensors"))
+
+
+@pytest.fixture(scope="module")
+def arena(cuda, meta):
+    """One pinned, seeded host arena (its layout is the same for every plan)."""
+
+    import layer_streaming as ls
+
+    plan = ls.build_llama31_8b_plan("matrix_group")
+    store = ls.create_weight_store(plan, "full_pinned")
+    store.fill_seeded(seed=meta["weight_seed"], device=cuda)
+    return store
+
+
+def make_store(arena, plan):
+    import layer_streaming as ls
+
+    store = ls.create_weight_store(plan, "full_pinned", allocate=False)
+    assert plan.host_arena_elements == arena.plan.host_arena_elements
+    store.arena = arena.arena
+    store._loaded = True
+    return store
+
+
+@pytest.fixture(scope="module")
+def hbm_engine(cuda, arena):
+    import layer_streaming as ls
+
+    plan = ls.build_llama31_8b_plan("matrix_group")
+    store = make_store(arena, plan)
+    resident = ls.ResidentDeviceArena(plan, store, cuda)
+    runtime = ls.DoubleBufferRuntime(plan, store, resident, cuda, weights="hbm")
+    return plan, store, resident, runtime
+
+
+def generate(executor, runtime, ids, steps):
+    """The tools/run_llama31.py loop; returns per-step (values, indices, logits)."""
+
+    out = []
+    with torch.inference_mode():
+        for _ in range(steps):
+            state = executor.begin(ids)
+            state = runtime.run(executor, state)
+            state = executor.finish(state)
+            out.append((
+                state.topk_values.reshape(-1).cpu(),
+                state.topk_indices.reshape(-1).cpu(),
+                None if state.logits is None else state.logits.reshape(-1).cpu(),
+            ))
+            ids = state.topk_indices[..., 0]
+    executor.check_errors()
+    return out
+
+
+def check_against_golden(results, meta):
+    """Top-k values within rtol/atol 2e-2, ranks identical where the logit
+    gaps around them exceed that tolerance, greedy ids identical (8 steps)."""
+
+    for step, ((values, indices, _), record) in enumerate(zip(results, meta["steps"])):
+        ref_v = torch.tensor(record["topk_values"])
+        torch.testing.assert_close(values, ref_v, rtol=RTOL, atol=ATOL)
+        for j in range(len(ref_v)):
+            tol = ATOL + RTOL * abs(float(ref_v[j]))
+            before = float(ref_v[j - 1] - ref_v[j]) if j else float("inf")
+            after = float(ref_v[j] - ref_v[j + 1]) if j + 1 < len(ref_v) else record["k_k1_gap"]
+            if before > tol and after > tol:
+                assert int(indices[j]) == record["topk_indices"][j], (step, j)
+        if step < 8:
+            assert int(indices[0]) == meta["greedy_ids"][step], "greedy id differs at step {}".format(step)
+
+
+def logit_stats(a, b):
+    d = (a - b).abs()
+    cos = float(torch.nn.functional.cosine_similarity(a.view(1, -1), b.view(1, -1)))
+    return {"max": float(d.max()), "mean": float(d.mean()), "rmse": float(d.pow(2).mean().sqrt()), "cos": cos}
+
+
+def test_config0_parity_with_reference(cuda, hbm_engine, meta, golden):
+    """Engine (HBM weights, graph replay) vs the reference's run (golden, CPU)
+    and vs the reference's PyTorch ops on this GPU (oracle), both fed the
+    reference's token path. Full logits use the reference's own comparison
+    metrics (benchmarks/compare_real_logits.py: max-abs, RMSE, cosine, top-10):
+    the engine must sit within the reference's GPU-vs-CPU noise floor."""
+
+    import layer_streaming as ls
+
+    plan, store, resident, runtime = hbm_engine
+    weights = dict(resident.views)
+    for index in range(len(plan.units)):
+        weights.update(runtime.unit_views(index))
+    oracle = lo.OracleDecoder(weights, top_k=meta["top_k"])
+    executor = ls.Llama31DecodeExecutor(Config(), resident, top_k=meta["top_k"], return_full_logits=True)
+    results = []
+    with torch.inference_mode():
+        for step, record in enumerate(meta["steps"]):
+            ids = torch.tensor([record["input_ids"]], device=cuda)
+            state = executor.finish(runtime.run(executor, executor.begin(ids)))
+            engine = state.logits.reshape(-1).float().cpu()
+            results.append((state.topk_values.reshape(-1).cpu(), state.topk_indices.reshape(-1).cpu(), engine))
+            reference_gpu = oracle.step(ids)["logits"][0, -1].float().cpu()
+            reference_cpu = golden["step{}.logits".format(step)].float()
+            e_c = logit_stats(engine, reference_cpu)
+            g_c = logit_stats(reference_gpu, reference_cpu)
+            e_g = logit_stats(engine, reference_gpu)
+            print("step {}: engine-vs-refCPU {} | refGPU-vs-refCPU {} | engine-vs-refGPU {}".format(
+                step, {k: round(v, 5) for k, v in e_c.items()}, {k: round(v, 5) for k, v in g_c.items()},
+                {k: round(v, 5) for k, v in e_g.items()}))
+            for stats in (e_c, e_g):
+                assert stats["cos"] > 0.9995
+                assert stats["max"] <= 1.5 * g_c["max"] + 0.05
+                assert stats["rmse"] <= 1.5 * g_c["rmse"]
+            top_engine = set(torch.topk(engine, 10).indices.tolist())
+            assert len(top_engine & set(record["topk_indices"])) >= 8
+    executor.check_errors()
+    check_against_golden(results, meta)
+
+
+def test_config0_greedy_generation(cuda, hbm_engine, meta):
+    """The tools/run_llama31.py loop on the engine's own greedy path."""
+
+    import layer_streaming as ls
+
+    plan, store, resident, runtime = hbm_engine
+    executor = ls.Llama31DecodeExecutor(Config(), resident, top_k=meta["top_k"])
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    results = generate(executor, runtime, ids, 1 + meta["decode_steps"])
+    check_against_golden(results, meta)
+    assert [int(r[1][0]) for r in results][:8] == meta["greedy_ids"][:8]
+
+
+def test_eager_and_graph_replay_are_identical(cuda, hbm_engine, meta):
+    import layer_streaming as ls
+
+    plan, store, resident, runtime = hbm_engine
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    runs = []
+    for graphs in (True, False):
+        executor = ls.Llama31DecodeExecutor(
+            Config(), resident, top_k=meta["top_k"], return_full_logits=True, use_graphs=graphs
+        )
+        runs.append(generate(executor, runtime, ids, 5))
+    for (v1, i1, l1), (v2, i2, l2) in zip(*runs):
+        assert torch.equal(v1, v2) and torch.equal(i1, i2) and torch.equal(l1, l2)
+
+
+def test_streamed_runtime_and_vocab_match(cuda, arena, hbm_engine, meta):
+    """The reference's own mode: H2D two-slot streaming + streamed vocab."""
+
+    import layer_streaming as ls
+
+    plan = ls.build_llama31_8b_plan("matrix_group", stream_vocab=True)
+    store = make_store(arena, plan)
+    resident = ls.ResidentDeviceArena(plan, store, cuda)
+    runtime = ls.DoubleBufferRuntime(plan, store, resident, cuda, profile=True)
+    vocab = ls.VocabStreamingRuntime(plan, store, runtime, profile=True)
+    executor = ls.Llama31DecodeExecutor(Config(), resident, vocab_runtime=vocab, top_k=meta["top_k"],
+                                        return_full_logits=True)
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    streamed = generate(executor, runtime, ids, 3)
+    check_against_golden(streamed, meta)
+    assert runtime.last_profile["h2d_bytes"] == plan.stream_bytes_per_token
+    assert vocab.last_profile["chunk_count"] == 8
+
+    # same bits as the hbm-resident engine (same kernels; only the LM-head
+    # kernel runs per chunk, and chunking does not change any logit)
+    _, _, hbm_resident, hbm_runtime = hbm_engine
+    hbm = ls.Llama31DecodeExecutor(Config(), hbm_resident, top_k=meta["top_k"], return_full_logits=True)
+    resident_run = generate(hbm, hbm_runtime, ids, 3)
+    for (v1, i1, l1), (v2, i2, l2) in zip(streamed, resident_run):
+        assert torch.equal(v1, v2) and torch.equal(i1, i2) and torch.equal(l1, l2)
+
+
+@pytest.mark.parametrize("granularity", ["matrix", "layer"])
+def test_other_granularities_give_same_tokens(cuda, arena, hbm_engine, meta, granularity):
+    import layer_streaming as ls
+
+    plan = ls.build_llama31_8b_plan(granularity)
+    store = make_store(arena, plan)
+    resident = ls.ResidentDeviceArena(plan, store, cuda)
+    runtime = ls.DoubleBufferRuntime(plan, store, resident, cuda, weights="streamed")
+    executor = ls.Llama31DecodeExecutor(Config(), resident, top_k=meta["top_k"], return_full_logits=True)
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    got = generate(executor, runtime, ids, 2)
+    _, _, hbm_resident, hbm_runtime = hbm_engine
+    ref = generate(ls.Llama31DecodeExecutor(Config(), hbm_resident, top_k=meta["top_k"], return_full_logits=True),
+                   hbm_runtime, ids, 2)
+    for (v1, i1, l1), (v2, i2, l2) in zip(got, ref):
+        assert torch.equal(i1, i2) and torch.equal(l1, l2)
+
+
+def test_slot_reuse_waits_for_compute(cuda, arena, meta):
+    """Race check of the two-slot protocol: delay every unit's compute; the
+    copy stream must still wait for the slot to be released (same results)."""
+
+    import layer_streaming as ls
+
+    plan = ls.build_llama31_8b_plan("matrix_group", stream_vocab=True)
+    store = make_store(arena, plan)
+    resident = ls.ResidentDeviceArena(plan, store, cuda)
+    runtime = ls.DoubleBufferRuntime(plan, store, resident, cuda)
+    vocab = ls.VocabStreamingRuntime(plan, store, runtime)
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    plain = ls.Llama31DecodeExecutor(Config(), resident, vocab_runtime=vocab, top_k=meta["top_k"])
+    base = generate(plain, runtime, ids, 2)
+
+    class Slow:
+        def __init__(self, inner):
+            self.inner = inner
+
+        def __call__(self, unit, weights, state):
+            torch.cuda._sleep(2_000_000)  # ~1 ms of GPU time before the unit's kernels
+            return self.inner(unit, weights, state)
+
+    slow_exec = ls.Llama31DecodeExecutor(Config(), resident, vocab_runtime=vocab, top_k=meta["top_k"])
+    slow = []
+    with torch.inference_mode():
+        state_ids = ids
+        for _ in range(2):
+            state = slow_exec.begin(state_ids)
+            state = runtime.run(Slow(slow_exec), state)
+            state = slow_exec.finish(state)
+            slow.append((state.topk_values.reshape(-1).cpu(), state.topk_indices.reshape(-1).cpu()))
+            state_ids = state.topk_indices[..., 0]
+    for (v1, i1, _), (v2, i2) in zip(base, slow):
+        assert torch.equal(v1, v2) and torch.equal(i1, i2)
