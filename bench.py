@@ -44,6 +44,17 @@ NORM_BYTES = 532_480
 GATE_UP_BYTES = 234_881_024
 
 
+# algorithmic bytes per launch of the kernels timed by --micro
+MICRO_BYTES = {
+    "qkv": 6144 * 4096 * 2,
+    "o_proj": 4096 * 4096 * 2,
+    "gate_up": GATE_UP_BYTES,
+    "down_proj": 4096 * 14336 * 2,
+    "lm_head": HEAD_BYTES,
+    "attention": 8 * 2048 * 128 * 2 * 2,
+}
+
+
 def step_bytes(context):
     """Algorithmic HBM bytes of one decode token at `context` cached positions."""
 
@@ -59,6 +70,11 @@ def parse_args():
     parser.add_argument("--context", type=int, default=2048)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--profile-range", action="store_true",
+                        help="after warm-up, run --steps decode steps between cudaProfilerStart/Stop "
+                             "(for `ncu --profile-from-start off`) and exit")
+    parser.add_argument("--micro", choices=sorted(MICRO_BYTES),
+                        help="time one kernel alone on a small footprint (rotating copies > L2)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -278,6 +294,76 @@ def cpu_baseline(store, executor, context, budget_s):
     }
 
 
+def micro(args, device):
+    """One kernel, back to back over rotating weight copies (> L2 in total)."""
+
+    from layer_streaming import _native, ops
+    from layer_streaming.llama31 import attention_split
+
+    _native.check(_native.lib().cb_prepare(), "cb_prepare")
+    bf = torch.bfloat16
+    name = args.micro
+    copies = {"lm_head": 2, "gate_up": 2}.get(name, 6)
+
+    def rnd(*shape, std=0.02):
+        return (torch.randn(shape, device=device) * std).to(bf)
+
+    x = rnd(4096, std=1.0)
+    norm = torch.ones(4096, dtype=bf, device=device)
+    if name == "qkv":
+        mats = [(rnd(4096, 4096), rnd(1024, 4096), rnd(1024, 4096)) for _ in range(copies)]
+        inv = torch.ones(64, device=device)
+        pos = torch.zeros(1, dtype=torch.int32, device=device)
+        q = torch.empty(4096, dtype=bf, device=device)
+        kc = torch.empty((8, 64, 128), dtype=bf, device=device)
+        vc = torch.empty_like(kc)
+        run = lambda m: ops.qkv_rope(x, norm, 1e-5, m[0], m[1], m[2], inv, pos, 0, q, kc, vc)
+    elif name in ("o_proj", "down_proj"):
+        k = 4096 if name == "o_proj" else 14336
+        xin = rnd(k, std=1.0)
+        mats = [rnd(4096, k) for _ in range(copies)]
+        res = rnd(4096, std=1.0)
+        run = lambda m: ops.proj_residual(xin, m, res, res)
+    elif name == "gate_up":
+        mats = [(rnd(14336, 4096), rnd(14336, 4096)) for _ in range(copies)]
+        out = torch.empty(14336, dtype=bf, device=device)
+        run = lambda m: ops.gate_up_swiglu(x, norm, 1e-5, m[0], m[1], out)
+    elif name == "lm_head":
+        mats = [rnd(128256, 4096) for _ in range(copies)]
+        values = torch.empty(10, device=device)
+        indices = torch.empty(10, dtype=torch.int64, device=device)
+        ws = torch.empty(ops.lm_head_workspace_bytes(10), dtype=torch.uint8, device=device)
+        ticket = torch.zeros(1, dtype=torch.int32, device=device)
+        run = lambda m: ops.lm_head_topk(x, norm, 1e-5, m, 0, 10, None, values, indices, ws, ticket)
+    else:  # attention, one decode token at args.context positions
+        cap = args.context + 64
+        mats = [(rnd(8, cap, 128, std=1.0), rnd(8, cap, 128, std=1.0)) for _ in range(64)]
+        q = rnd(4096, std=1.0)
+        pos = torch.tensor([args.context - 1], dtype=torch.int32, device=device)
+        splits, chunk = attention_split(1, args.context, torch.cuda.get_device_properties(device).multi_processor_count)
+        ws = torch.empty(ops.attention_workspace_bytes(1, splits), dtype=torch.uint8, device=device)
+        tickets = torch.zeros(8, dtype=torch.int32, device=device)
+        out = torch.empty(4096, dtype=bf, device=device)
+        run = lambda m: ops.attention(q, m[0], m[1], pos, splits, chunk, out, ws, tickets)
+    for i in range(args.warmup * len(mats)):
+        run(mats[i % len(mats)])
+    torch.cuda.synchronize()
+    launches = args.steps * len(mats)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(launches):
+        run(mats[i % len(mats)])
+    end.record()
+    torch.cuda.synchronize()
+    us = start.elapsed_time(end) * 1000.0 / launches
+    nbytes = MICRO_BYTES[name] if name != "attention" else 8 * args.context * 128 * 2 * 2
+    peak, kind = measured_peak()
+    gbs = nbytes / (us * 1e-6) / 1e9
+    print(json.dumps({"micro": name, "us_per_launch": round(us, 3), "bytes_per_launch": nbytes,
+                      "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "peak_kind": kind,
+                      "frac": round(gbs / peak, 4), "launches": launches, "copies": len(mats)}), flush=True)
+
+
 def reference_arm(args, rank):
     """--impl reference: the reference's CPU algorithm on this host's cores."""
 
@@ -337,6 +423,9 @@ def main():
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.micro:
+        micro(args, device)
+        return
     group = None
     if world > 1:
         import datetime
@@ -353,6 +442,18 @@ def main():
     extra = args.warmup + args.steps * 2 + 64
     plan, store, resident, runtime, executor = build_engine(device, args.context, extra)
     token = prefill(executor, runtime, device, args.context)
+    if args.profile_range:
+        with torch.inference_mode():
+            for _ in range(args.warmup):
+                token = step(executor, runtime, token).topk_indices[..., 0]
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStart()
+            for _ in range(args.steps):
+                token = step(executor, runtime, token).topk_indices[..., 0]
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStop()
+        print(json.dumps({"profile_range": args.steps, "context": args.context}), flush=True)
+        return
     clocks = ClockSampler(local)
     clocks.start()
     ms, token = time_decode(executor, runtime, token, args.steps, args.warmup, barrier)

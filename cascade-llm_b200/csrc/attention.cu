@@ -53,8 +53,11 @@ struct AttnSmem {
   static constexpr size_t BAR_OFF = V_OFF + kAttnStages * STAGE;         // full, empty
   static constexpr size_t SC_OFF = BAR_OFF + 2 * kAttnStages * 8;       // [2][4][64] fp32
   static constexpr size_t ST_OFF = SC_OFF + 2 * kGroup * kSub * 4;      // alpha[2][4], m[4], l[4]
-  static constexpr size_t RED_OFF = ST_OFF + 16 * 4;                    // [4 pg][4 h][128] fp32
-  static constexpr size_t BYTES = RED_OFF + 4 * kGroup * kHeadDim * 4;
+  static constexpr size_t RED_OFF = ST_OFF + 16 * 4;                    // o merge / split merge
+  static constexpr size_t RED_FLOATS = 4 * kGroup * kHeadDim > 2 * kGroup * 256 + 3 * kGroup
+                                           ? 4 * kGroup * kHeadDim
+                                           : 2 * kGroup * 256 + 3 * kGroup;
+  static constexpr size_t BYTES = RED_OFF + RED_FLOATS * 4;
 };
 
 __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid_constant__ AttnParams p) {
@@ -252,20 +255,69 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
   named_sync(1, kAttnConsumers);
   if (__float_as_int(red[0]) != 1) return;
   __threadfence();
-  for (int e = tid; e < kGroup * kHeadDim; e += kAttnConsumers) {
-    const int h = e / kHeadDim, d = e % kHeadDim;
-    const int64_t base = (int64_t(m) * 32 + g * kGroup + h) * p.splits;
-    float mx = -__int_as_float(0x7F800000);
-    for (int j = 0; j < p.splits; ++j) mx = fmaxf(mx, __ldcg(p.part_ml + (base + j) * 2));
-    float num = 0.f, den = 0.f;
-    for (int j = 0; j < p.splits; ++j) {
-      const float mj = __ldcg(p.part_ml + (base + j) * 2);
-      if (mj == -__int_as_float(0x7F800000)) continue;  // empty split
-      const float w = expf(mj - mx);
-      den = fmaf(w, __ldcg(p.part_ml + (base + j) * 2 + 1), den);
-      num = fmaf(w, __ldcg(p.part_o + (base + j) * kHeadDim + d), num);
+  // Last CTA of the group: merge the splits. The per-split (max, sum) pairs
+  // of the 4 heads are staged in shared memory in blocks of 256 splits (all
+  // loads issued in parallel), then each thread reduces its 2 outputs over
+  // the splits with independent, unrolled loads.
+  float* st_m = red;                         // [4][256] running maxima
+  float* st_w = red + kGroup * 256;          // [4][256] weights exp(m_s - M)
+  float* st_l = red + 2 * kGroup * 256;      // [4] combined denominators
+  float* st_M = st_l + kGroup;               // [4] combined maxima
+  float* st_s = st_M + kGroup;               // [4] rescale factor of this block
+  if (tid < kGroup) {
+    st_M[tid] = -__int_as_float(0x7F800000);
+    st_l[tid] = 0.f;
+  }
+  float acc[2] = {0.f, 0.f};
+  const int e0 = tid, e1 = tid + kAttnConsumers;  // outputs (h, d) = e / 128, e % 128
+  for (int base = 0; base < p.splits; base += 256) {
+    const int nb = min(256, p.splits - base);
+    named_sync(1, kAttnConsumers);
+    for (int i = tid; i < kGroup * nb; i += kAttnConsumers) {
+      const int h = i / nb, j = i % nb;
+      st_m[h * 256 + j] = __ldcg(p.part_ml + ((int64_t(m) * 32 + g * kGroup + h) * p.splits + base + j) * 2);
     }
-    p.out[int64_t(m) * 4096 + (g * kGroup + h) * kHeadDim + d] = f2bf(num / den);
+    named_sync(1, kAttnConsumers);
+    if (warp < kGroup) {  // warp h: new running max and rescale of the previous blocks
+      float mx = -__int_as_float(0x7F800000);
+      for (int j = lane; j < nb; j += 32) mx = fmaxf(mx, st_m[warp * 256 + j]);
+      mx = warp_max(mx);
+      const float mold = st_M[warp], mnew = fmaxf(mold, mx);
+      float lsum = 0.f;
+      for (int j = lane; j < nb; j += 32) {
+        const float mj = st_m[warp * 256 + j];
+        const float w = mj == -__int_as_float(0x7F800000) ? 0.f : expf(mj - mnew);
+        st_w[warp * 256 + j] = w;
+        lsum = fmaf(w, __ldcg(p.part_ml + ((int64_t(m) * 32 + g * kGroup + warp) * p.splits + base + j) * 2 + 1),
+                    lsum);
+      }
+      lsum = warp_sum(lsum);
+      if (lane == 0) {
+        const float scale = mold == -__int_as_float(0x7F800000) ? 0.f : expf(mold - mnew);
+        st_l[warp] = st_l[warp] * scale + lsum;
+        st_M[warp] = mnew;
+        st_s[warp] = scale;  // rescale of the earlier blocks
+      }
+    }
+    named_sync(1, kAttnConsumers);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int e = q ? e1 : e0;
+      const int h = e / kHeadDim, d = e % kHeadDim;
+      acc[q] *= st_s[h];
+      const float* po = p.part_o + ((int64_t(m) * 32 + g * kGroup + h) * p.splits + base) * kHeadDim + d;
+      float sum = 0.f;
+#pragma unroll 8
+      for (int j = 0; j < nb; ++j) sum = fmaf(st_w[h * 256 + j], __ldcg(po + int64_t(j) * kHeadDim), sum);
+      acc[q] += sum;
+    }
+  }
+  named_sync(1, kAttnConsumers);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int e = q ? e1 : e0;
+    const int h = e / kHeadDim, d = e % kHeadDim;
+    p.out[int64_t(m) * 4096 + (g * kGroup + h) * kHeadDim + d] = f2bf(acc[q] / st_l[h]);
   }
   if (tid == 0) p.tickets[m * 8 + g] = 0u;
 }

@@ -30,11 +30,18 @@
 //     conflicts) and the reduction is one warp shuffle tree + WPR partials.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 #include "cascade_b200.h"
 
 namespace cb {
+
+// Every GEMV launch is two CTAs per SM (one full wave at <= 128 registers
+// per thread); the LM-head candidate workspace is sized by the same grid.
+static int gemv_grid() { return 2 * sm_count(); }
+static int lm_head_grid() { return gemv_grid(); }
 
 enum EpiMode : int {
   EPI_STORE = 0,     // out[oA] = bf16(a), out[oB] = bf16(b)
@@ -46,10 +53,9 @@ enum EpiMode : int {
   EPI_TOPK = 6,      // fp32 logits of bf16(acc) -> running top-k
 };
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;
+constexpr int kThreads = 256;
 constexpr int kTopkMax = 64;
+constexpr size_t kMaxSmem = 227 * 1024;
 
 struct Segment {
   const uint16_t* a_base;  // weight row base of slab A rows
@@ -88,41 +94,6 @@ struct GemvParams {
   int* err;
 };
 
-// ---------------------------------------------------------------- tiles
-// A CTA walks units [u0, u1) in tiles of <= T units that never cross a
-// segment or group boundary; producer and consumers walk the same sequence.
-struct TileWalker {
-  int u, u1, seg, seg_start;
-  __device__ void begin(const GemvParams& p, int first, int last) {
-    u = first;
-    u1 = last;
-    seg = 0;
-    seg_start = 0;
-    while (seg < p.nseg && u >= seg_start + p.seg[seg].units) {
-      seg_start += p.seg[seg].units;
-      ++seg;
-    }
-  }
-  // returns false when done; else segment index, local unit j0, count t
-  template <int T>
-  __device__ bool next(const GemvParams& p, int& s, int& j0, int& t) {
-    if (u >= u1) return false;
-    while (u >= seg_start + p.seg[seg].units) {
-      seg_start += p.seg[seg].units;
-      ++seg;
-    }
-    const Segment& sg = p.seg[seg];
-    j0 = u - seg_start;
-    int left_group = sg.group - (j0 % sg.group);
-    int left_seg = sg.units - j0;
-    int left_cta = u1 - u;
-    t = min(T, min(left_group, min(left_seg, left_cta)));
-    s = seg;
-    u += t;
-    return true;
-  }
-};
-
 __device__ __forceinline__ int64_t unit_row(const Segment& s, int j) {
   return int64_t(j / s.group) * s.group_stride + (j % s.group);
 }
@@ -131,18 +102,76 @@ __device__ __forceinline__ bool ranks_before(float va, int64_t ia, float vb, int
   return va > vb || (va == vb && ia < ib);
 }
 
-// Insert (v, i) into a sorted list of length *n (capacity k).
-__device__ void topk_insert(float* vals, int64_t* idx, int& n, int k, float v, int64_t i) {
-  if (n == k && !ranks_before(v, i, vals[k - 1], idx[k - 1])) return;
-  int pos = n < k ? n : k - 1;
-  while (pos > 0 && ranks_before(v, i, vals[pos - 1], idx[pos - 1])) {
-    vals[pos] = vals[pos - 1];
-    idx[pos] = idx[pos - 1];
-    --pos;
+// Warp-cooperative exact top-k over n (value, index) pairs in shared memory.
+__device__ void warp_select_rows_idx(const float* vals, const int64_t* idx, int n, int k, float* out_v,
+                                     int64_t* out_i) {
+  const int lane = threadIdx.x & 31;
+  float pv = __int_as_float(0x7F800000);
+  int64_t pi = -1;
+  for (int r = 0; r < k; ++r) {
+    float bv = -__int_as_float(0x7F800000);
+    int64_t bi = INT64_MAX;
+    for (int c = lane; c < n; c += 32) {
+      const float v = vals[c];
+      const int64_t i = idx[c];
+      if (ranks_before(pv, pi, v, i) && ranks_before(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+      const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (ranks_before(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      out_v[r] = bv;
+      out_i[r] = bi;
+    }
+    pv = bv;
+    pi = bi;
   }
-  vals[pos] = v;
-  idx[pos] = i;
-  if (n < k) ++n;
+}
+
+// Warp-cooperative exact top-k over a CTA's logits in shared memory:
+// entry i < na is row a0 + i, entry i >= na is row b0 + (i - na). Missing
+// entries (n < k) are written as (-inf, INT64_MAX).
+__device__ void warp_select_rows(const float* vals, int n, int na, int64_t a0, int64_t b0, int k,
+                                 float* out_v, int64_t* out_i) {
+  const int lane = threadIdx.x & 31;
+  float pv = __int_as_float(0x7F800000);
+  int64_t pi = -1;
+  for (int r = 0; r < k; ++r) {
+    float bv = -__int_as_float(0x7F800000);
+    int64_t bi = INT64_MAX;
+    for (int c = lane; c < n; c += 32) {
+      const float v = vals[c];
+      const int64_t i = c < na ? a0 + c : b0 + (c - na);
+      if (ranks_before(pv, pi, v, i) && ranks_before(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+      const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (ranks_before(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      out_v[r] = bv;
+      out_i[r] = bi;
+    }
+    pv = bv;
+    pi = bi;
+  }
 }
 
 // Warp-cooperative exact top-k of n candidates; lane 0 writes the result.
@@ -184,44 +213,75 @@ __device__ void warp_select_topk(const float* vals, const int64_t* idx, int n, i
   }
 }
 
+// Exact top-k of G sorted per-CTA candidate lists (k each, in global
+// memory), by the whole CTA. The k-th best of the union is at least the
+// largest per-list k-th value, so only candidates at or above that
+// threshold can qualify: one parallel pass finds the threshold, a second
+// copies the survivors to shared memory, and warp 0 selects among them.
+// `scratch` must hold kMergeCap floats + kMergeCap int64s.
+constexpr int kMergeCap = 1024;
+__device__ void block_merge_topk(const float* vals, const int64_t* idx, int G, int k, float* out_v,
+                                 int64_t* out_i, float* red, float* scratch) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float thr = -__int_as_float(0x7F800000);
+  for (int c = tid; c < G; c += blockDim.x) thr = fmaxf(thr, __ldcg(vals + size_t(c) * k + (k - 1)));
+  thr = warp_max(thr);
+  __syncthreads();
+  if (lane == 0) red[warp] = thr;
+  int* count = reinterpret_cast<int*>(red + 14);
+  if (tid == 0) *count = 0;
+  __syncthreads();
+  thr = red[0];
+  for (int q = 1; q < int(blockDim.x >> 5); ++q) thr = fmaxf(thr, red[q]);
+  float* sv = scratch;
+  int64_t* si = reinterpret_cast<int64_t*>(scratch + kMergeCap);
+  const int n = G * k;
+  for (int c = tid; c < n; c += blockDim.x) {
+    const float v = __ldcg(vals + c);
+    if (v >= thr) {
+      const int slot = atomicAdd(count, 1);
+      if (slot < kMergeCap) {
+        sv[slot] = v;
+        si[slot] = __ldcg(reinterpret_cast<const long long*>(idx) + c);
+      }
+    }
+  }
+  __syncthreads();
+  const int kept = *count;
+  if (warp == 0) {
+    if (kept <= kMergeCap)
+      warp_select_rows_idx(sv, si, kept, k, out_v, out_i);
+    else  // pathological ties: fall back to scanning every candidate
+      warp_select_topk(vals, idx, n, k, out_v, out_i);
+  }
+}
+
+
 }  // namespace cb
 
 namespace cb {
 
-template <int K, int KT, int T, int NSTAGE, bool XS>
-struct GemvCfg {
-  static constexpr int R = 2 * T;                  // weight rows per tile
-  static constexpr int WPR = kConsumerWarps / R;   // warps per row
-  static constexpr int KSEG = KT / WPR;            // K elements per warp per K-tile
-  static constexpr int KPL = KSEG / 256;           // uint4 (8 bf16) per lane per K-tile
-  static constexpr int NKT = K / KT;               // K-tiles per row
-  static constexpr int STAGE_ELEMS = R * KT;
-  static constexpr size_t RING = size_t(NSTAGE) * STAGE_ELEMS * 2;
-  static constexpr size_t BARS = RING;                               // full[NSTAGE], empty[NSTAGE]
-  static constexpr size_t PART = BARS + 2 * NSTAGE * 8;              // [2][R][WPR] fp32
-  static constexpr size_t RED = PART + 2 * R * WPR * 4;              // [8] fp32 + flag
-  static constexpr size_t TOPV = (RED + 16 * 4 + 15) / 16 * 16;      // [kTopkMax] fp32
-  static constexpr size_t TOPI = TOPV + kTopkMax * 4;                // [kTopkMax] int64
-  static constexpr size_t XSM = TOPI + kTopkMax * 8;                 // [K] bf16 when XS
-  static constexpr size_t SMEM = XSM + (XS ? size_t(K) * 2 : 0);
-  static_assert(kConsumerWarps % R == 0, "rows per tile must divide the consumer warps");
-  static_assert(KSEG % 256 == 0 && KPL >= 1, "K-tile must split into whole 512-byte warp reads");
-  static_assert(K % KT == 0, "K-tiles must cover K");
-  static_assert((KT * 2) % 16 == 0, "bulk copies move multiples of 16 bytes");
-};
-
 __device__ __forceinline__ uint4 normalize8(uint4 xu, uint4 wu, float inv) {
-  uint32_t in[4] = {xu.x, xu.y, xu.z, xu.w};
-  uint32_t wv[4] = {wu.x, wu.y, wu.z, wu.w};
+  const uint32_t in[4] = {xu.x, xu.y, xu.z, xu.w};
+  const uint32_t wv[4] = {wu.x, wu.y, wu.z, wu.w};
   uint32_t out[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     // llama31.py:21-25: bf16(x * rsqrt(...)), then bf16(w * that)
-    float lo = rbf(bf16lo(wv[q]) * rbf(bf16lo(in[q]) * inv));
-    float hi = rbf(bf16hi(wv[q]) * rbf(bf16hi(in[q]) * inv));
+    const float lo = rbf(bf16lo(wv[q]) * rbf(bf16lo(in[q]) * inv));
+    const float hi = rbf(bf16hi(wv[q]) * rbf(bf16hi(in[q]) * inv));
     out[q] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
   }
   return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// Loads of weights that are read exactly once: 128-bit, not cached in L1.
+__device__ __forceinline__ uint4 ld_stream(const uint16_t* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
 }
 
 __device__ __forceinline__ float silu_bf16(float g) {
@@ -276,208 +336,172 @@ __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int j, flo
   }
 }
 
-// Two CTAs of 288 threads x 112 registers fit one SM's 64K registers, so a
-// kernel's CTAs can share an SM with the next kernel's early-launched ones.
-template <int K, int KT, int T, int NSTAGE, bool XS>
-__global__ void __maxnreg__(112)
-    gemv_kernel(const __grid_constant__ GemvParams p) {
-  using C = GemvCfg<K, KT, T, NSTAGE, XS>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint16_t* ring = reinterpret_cast<uint16_t*>(smem);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BARS);
-  uint64_t* empty = full + NSTAGE;
-  float* partial = reinterpret_cast<float*>(smem + C::PART);
-  float* red = reinterpret_cast<float*>(smem + C::RED);
-  float* topv = reinterpret_cast<float*>(smem + C::TOPV);
-  int64_t* topi = reinterpret_cast<int64_t*>(smem + C::TOPI);
-  uint16_t* xsm = reinterpret_cast<uint16_t*>(smem + C::XSM);
+template <int K>
+struct GemvShape {
+  static constexpr int WARPS = kThreads / 32;
+  static constexpr int KS = K / WARPS;          // K-slice of each warp
+  static constexpr int CPL = KS / 256;          // 16-byte chunks per lane per row slice
+  static constexpr int UB = (16 / (2 * CPL)) > 0 ? 16 / (2 * CPL) : 1;  // units per batch
+  static constexpr size_t RED = 0;              // [16] fp32 (norm partials, flag)
+  static constexpr size_t SMEM = RED + 16 * 4;  // + per-unit partials (+ logits), sized at launch
+  static_assert(KS % 256 == 0, "each warp's K-slice must be whole 512-byte lane groups");
+};
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// CTA-cooperative split-K GEMV. A CTA owns a contiguous range of units (row
+// pairs); each of its 8 warps streams its own 1/8 of K for EVERY unit of the
+// range (UB units, i.e. 2*UB*CPL 128-bit loads per lane, in flight per
+// batch), so all warps carry the same load and stream until the end. Per
+// unit, each warp reduces its two partial dots with shuffles into shared
+// memory; after ONE barrier the epilogues of all units run in parallel, one
+// thread per unit. The activation slice of a warp stays in registers. The
+// first batch of weight loads is issued before griddepcontrol.wait.
+template <int K>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
+  using S = GemvShape<K>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* red = reinterpret_cast<float*>(smem + S::RED);
+  float* part = reinterpret_cast<float*>(smem + S::SMEM);  // [units][2][WARPS]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int G = gridDim.x;
   const int u0 = int(int64_t(p.total_units) * blockIdx.x / G);
   const int u1 = int(int64_t(p.total_units) * (blockIdx.x + 1) / G);
+  const int units = u1 - u0;
+  float* lrow = part + size_t(units) * 2 * S::WARPS;  // EPI_TOPK: this CTA's logits
+  const int kbase = warp * S::KS + lane * 8;            // first element of this lane
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < NSTAGE; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+  auto locate = [&](int u, int& seg, int& j) {
+    seg = 0;
+    j = u;
+    while (seg + 1 < p.nseg && j >= p.seg[seg].units) {
+      j -= p.seg[seg].units;
+      ++seg;
     }
-    fence_mbar_init();
-  }
-  __syncthreads();
-
-  if (warp == kConsumerWarps) {
-    // ---------------- producer: weights only, so no grid-dependency wait
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      TileWalker w;
-      w.begin(p, u0, u1);
-      int s, j0, t, stage = 0;
-      uint32_t phase = 0;
-      while (w.next<T>(p, s, j0, t)) {
-        const Segment& sg = p.seg[s];
-        const int64_t row = unit_row(sg, j0);
-        const uint16_t* a = sg.a_base + row * K;
-        const uint16_t* b = sg.b_base + row * K;
-        for (int kt = 0; kt < C::NKT; ++kt) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 101)) return;
-          uint16_t* dst = ring + size_t(stage) * C::STAGE_ELEMS;
-          mbar_arrive_expect_tx(&full[stage], uint32_t(2 * t * KT * 2));
-          if (KT == K) {
-            bulk_g2s_stream(dst, a, uint32_t(t * K * 2), &full[stage], pol);
-            bulk_g2s_stream(dst + T * KT, b, uint32_t(t * K * 2), &full[stage], pol);
-          } else {
-            for (int r = 0; r < t; ++r) {
-              bulk_g2s_stream(dst + r * KT, a + r * K + kt * KT, KT * 2, &full[stage], pol);
-              bulk_g2s_stream(dst + (T + r) * KT, b + r * K + kt * KT, KT * 2, &full[stage], pol);
-            }
-          }
-          if (++stage == NSTAGE) {
-            stage = 0;
-            phase ^= 1;
-          }
+  };
+  auto row_ptrs = [&](int u, const uint16_t*& ra, const uint16_t*& rb) {
+    int seg, j;
+    locate(u, seg, j);
+    const Segment& sg = p.seg[seg];
+    const int64_t row = int64_t(j / sg.group) * sg.group_stride + (j % sg.group);
+    ra = sg.a_base + row * K + kbase;
+    rb = sg.b_base + row * K + kbase;
+  };
+  uint4 w[S::UB][2][S::CPL];
+  auto load_batch = [&](int ub) {
+#pragma unroll
+    for (int i = 0; i < S::UB; ++i) {
+      if (ub + i < u1) {
+        const uint16_t *ra, *rb;
+        row_ptrs(ub + i, ra, rb);
+#pragma unroll
+        for (int c = 0; c < S::CPL; ++c) {
+          w[i][0][c] = ld_stream(ra + c * 256);
+          w[i][1][c] = ld_stream(rb + c * 256);
         }
       }
     }
-    return;
-  }
+  };
 
-  // ---------------- consumers
-  const int ctid = threadIdx.x;
-  grid_dep_wait();   // activations come from the previous kernel
-  if (ctid == 0) grid_dep_launch();
+  // weights do not depend on the previous kernel: start streaming now
+  load_batch(u0);
 
+  grid_dep_wait();  // the activation row comes from the previous kernel
+  if (tid == 0) grid_dep_launch();
   float inv = 1.0f;
   if (p.norm_w) {
     float ss = 0.f;
-    for (int c = ctid; c < K / 8; c += kConsumers) {
-      const uint4 u = ld_cg_u4(p.x + c * 8);
-      const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+    for (int c = tid; c < K / 8; c += kThreads) {
+      const uint4 v = ld_cg_u4(p.x + c * 8);
+      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float lo = bf16lo(v[q]), hi = bf16hi(v[q]);
-        ss = fmaf(lo, lo, ss);
-        ss = fmaf(hi, hi, ss);
+        ss = fmaf(bf16lo(w4[q]), bf16lo(w4[q]), ss);
+        ss = fmaf(bf16hi(w4[q]), bf16hi(w4[q]), ss);
       }
     }
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
-    named_sync(1, kConsumers);
+    __syncthreads();
     float tot = 0.f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
+    for (int q = 0; q < S::WARPS; ++q) tot += red[q];
     inv = rsqrtf(tot * (1.0f / K) + p.eps);
   }
-
-  const int r = warp / C::WPR, part = warp % C::WPR;
-  const int rr = r < T ? r : r - T;
-  // activation slice of this warp: registers (XS=false) or the whole row in
-  // shared memory (XS=true, for K=14336 where registers would spill)
-  uint4 xf[XS ? 1 : C::NKT][XS ? 1 : C::KPL];
-  if constexpr (XS) {
-    for (int c = ctid; c < K / 8; c += kConsumers) {
-      uint4 u = ld_cg_u4(p.x + c * 8);
-      if (p.norm_w) u = normalize8(u, __ldg(reinterpret_cast<const uint4*>(p.norm_w + c * 8)), inv);
-      reinterpret_cast<uint4*>(xsm)[c] = u;
-    }
-    named_sync(1, kConsumers);
-  } else {
+  uint4 xr[S::CPL];
 #pragma unroll
-    for (int kt = 0; kt < C::NKT; ++kt)
-#pragma unroll
-      for (int i = 0; i < C::KPL; ++i) {
-        const int k0 = kt * KT + part * C::KSEG + (lane + 32 * i) * 8;
-        uint4 u = ld_cg_u4(p.x + k0);
-        if (p.norm_w) u = normalize8(u, __ldg(reinterpret_cast<const uint4*>(p.norm_w + k0)), inv);
-        xf[kt][i] = u;
-      }
+  for (int c = 0; c < S::CPL; ++c) {
+    uint4 v = ld_cg_u4(p.x + kbase + c * 256);
+    if (p.norm_w) v = normalize8(v, __ldg(reinterpret_cast<const uint4*>(p.norm_w + kbase + c * 256)), inv);
+    xr[c] = v;
   }
-  const int pos = p.pos ? __ldcg(p.pos) + p.token : 0;
 
-  TileWalker w;
-  w.begin(p, u0, u1);
-  int s, j0, t, stage = 0, buf = 0, ntop = 0;
-  uint32_t phase = 0;
-  // A timed-out wait only records the error and stops further waiting: the
-  // control flow (and so every named barrier) stays identical in all threads.
-  bool failed = false;
-  while (w.next<T>(p, s, j0, t)) {
-    float acc = 0.f;
+  for (int ub = u0; ub < u1; ub += S::UB) {
+    if (ub != u0) load_batch(ub);
 #pragma unroll
-    for (int kt = 0; kt < C::NKT; ++kt) {
-      if (!failed && !mbar_wait(&full[stage], phase, p.err, 102)) failed = true;
-      if (rr < t) {
-        const uint4* wrow = reinterpret_cast<const uint4*>(ring + size_t(stage) * C::STAGE_ELEMS +
-                                                           r * KT + part * C::KSEG);
-        if constexpr (XS) {
-          const uint4* xrow = reinterpret_cast<const uint4*>(xsm + kt * KT + part * C::KSEG);
+    for (int i = 0; i < S::UB; ++i) {
+      if (ub + i < u1) {
+        float a = 0.f, b = 0.f;
 #pragma unroll
-          for (int i = 0; i < C::KPL; ++i) acc = dot8(wrow[lane + 32 * i], xrow[lane + 32 * i], acc);
-        } else {
-#pragma unroll
-          for (int i = 0; i < C::KPL; ++i) acc = dot8(wrow[lane + 32 * i], xf[kt][i], acc);
+        for (int c = 0; c < S::CPL; ++c) {
+          a = dot8(w[i][0][c], xr[c], a);
+          b = dot8(w[i][1][c], xr[c], b);
+        }
+        a = warp_sum(a);
+        b = warp_sum(b);
+        if (lane == 0) {
+          part[((ub + i - u0) * 2 + 0) * S::WARPS + warp] = a;
+          part[((ub + i - u0) * 2 + 1) * S::WARPS + warp] = b;
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-      if (++stage == NSTAGE) {
-        stage = 0;
-        phase ^= 1;
-      }
     }
-    acc = warp_sum(acc);
-    if (lane == 0) partial[(buf * C::R + r) * C::WPR + part] = acc;
-    named_sync(1, kConsumers);
-    const Segment& sg = p.seg[s];
+  }
+  __syncthreads();
+
+  const int pos = p.pos ? __ldcg(p.pos) + p.token : 0;
+  for (int i = tid; i < units; i += kThreads) {
+    float a = 0.f, b = 0.f;
+#pragma unroll
+    for (int q = 0; q < S::WARPS; ++q) {
+      a += part[(i * 2 + 0) * S::WARPS + q];
+      b += part[(i * 2 + 1) * S::WARPS + q];
+    }
+    int seg, j;
+    locate(u0 + i, seg, j);
+    const Segment& sg = p.seg[seg];
     if (sg.mode == EPI_TOPK) {
-      if (ctid == 0) {
-        for (int u = 0; u < t; ++u) {
-          float a = 0.f, b = 0.f;
-#pragma unroll
-          for (int q = 0; q < C::WPR; ++q) {
-            a += partial[(buf * C::R + u) * C::WPR + q];
-            b += partial[(buf * C::R + T + u) * C::WPR + q];
-          }
-          const int64_t oa = unit_row(sg, j0 + u), ob = oa + sg.b_offset;
-          const float la = rbf(a), lb = rbf(b);  // F.linear(...) is bf16, then .float()
-          if (p.logits) {
-            p.logits[oa] = la;
-            p.logits[ob] = lb;
-          }
-          topk_insert(topv, topi, ntop, p.k, la, p.row_offset + oa);
-          topk_insert(topv, topi, ntop, p.k, lb, p.row_offset + ob);
-        }
+      const float la = rbf(a), lb = rbf(b);  // F.linear(...) is bf16, then .float()
+      const int64_t row = int64_t(j / sg.group) * sg.group_stride + (j % sg.group);
+      if (p.logits) {
+        p.logits[row] = la;
+        p.logits[row + sg.b_offset] = lb;
       }
-    } else if (ctid < t) {
-      float a = 0.f, b = 0.f;
-#pragma unroll
-      for (int q = 0; q < C::WPR; ++q) {
-        a += partial[(buf * C::R + ctid) * C::WPR + q];
-        b += partial[(buf * C::R + T + ctid) * C::WPR + q];
-      }
-      gemv_epilogue(p, sg, j0 + ctid, a, b, pos);
+      lrow[i] = la;
+      lrow[units + i] = lb;
+    } else {
+      gemv_epilogue(p, sg, j, a, b, pos);
     }
-    buf ^= 1;
   }
 
   if (p.cand_values == nullptr) return;
-  // ---------------- LM head: publish this CTA's top-k, last CTA merges
-  if (ctid == 0) {
-    for (int i = 0; i < p.k; ++i) {
-      const bool have = i < ntop;
-      p.cand_values[size_t(blockIdx.x) * p.k + i] = have ? topv[i] : -__int_as_float(0x7F800000);
-      p.cand_indices[size_t(blockIdx.x) * p.k + i] = have ? topi[i] : INT64_MAX;
-    }
+  // ---------------- LM head: this CTA's exact top-k, then the last CTA merges
+  __syncthreads();
+  if (warp == 0) {
+    const int64_t half = p.seg[0].b_offset;
+    warp_select_rows(lrow, 2 * units, units, p.row_offset + u0, p.row_offset + half + u0, p.k,
+                     p.cand_values + size_t(blockIdx.x) * p.k, p.cand_indices + size_t(blockIdx.x) * p.k);
+  }
+  __syncthreads();
+  if (tid == 0) {
     __threadfence();
     const unsigned int ticket = atomicAdd(p.ticket, 1u);
-    red[8] = __int_as_float(ticket == unsigned(G - 1) ? 1 : 0);
+    red[15] = __int_as_float(ticket == unsigned(G - 1) ? 1 : 0);
   }
-  named_sync(1, kConsumers);
-  if (__float_as_int(red[8]) == 1 && warp == 0) {
-    __threadfence();
-    warp_select_topk(p.cand_values, p.cand_indices, G * p.k, p.k, p.out_values, p.out_indices);
-    if (lane == 0) *p.ticket = 0u;
-  }
+  __syncthreads();
+  if (__float_as_int(red[15]) != 1) return;
+  __threadfence();
+  block_merge_topk(p.cand_values, p.cand_indices, G, p.k, p.out_values, p.out_indices, red,
+                   reinterpret_cast<float*>(lrow));
+  if (tid == 0) *p.ticket = 0u;
 }
 
 }  // namespace cb
@@ -487,17 +511,24 @@ namespace cb {
 
 int32_t* error_word();
 
-template <int K, int KT, int T, int NSTAGE, bool XS = false>
+template <int K>
 static int run_gemv(const char* what, GemvParams& p, cudaStream_t stream) {
-  using C = GemvCfg<K, KT, T, NSTAGE, XS>;
-  auto kernel = gemv_kernel<K, KT, T, NSTAGE, XS>;
-  int rc = configure_smem(what, kernel, C::SMEM);
+  using S = GemvShape<K>;
+  int rc = configure_smem(what, gemv_kernel<K>, kMaxSmem);
   if (rc != kOk) return rc;
   p.total_units = 0;
   for (int i = 0; i < p.nseg; ++i) p.total_units += p.seg[i].units;
   if (p.total_units == 0) return kOk;
   p.err = error_word();
-  return launch(what, kernel, dim3(sm_count()), dim3(kThreads), C::SMEM, stream, p);
+  const int grid = gemv_grid();
+  const size_t per_cta = size_t((p.total_units + grid - 1) / grid);
+  size_t smem = S::SMEM + per_cta * 2 * S::WARPS * sizeof(float);  // per-unit partials
+  if (p.cand_values) {
+    // EPI_TOPK: the CTA's logits, later reused as the last CTA's merge scratch
+    smem += std::max(per_cta * 2 * sizeof(float), size_t(kMergeCap) * (sizeof(float) + sizeof(int64_t)));
+  }
+  if (smem > kMaxSmem) return fail(kErrInvalid, "%s: %zu units per CTA exceed shared memory", what, per_cta);
+  return launch(what, gemv_kernel<K>, dim3(grid), dim3(kThreads), smem, stream, p);
 }
 
 static Segment half_segment(const void* w, int N, int K, int mode, void* out, const void* aux) {
@@ -572,7 +603,7 @@ extern "C" int cb_qkv_rope(const void* x, const void* norm_w, float eps, const v
     CB_REQUIRE(aligned16(wv) && v_cache, "cb_qkv_rope: wv needs alignment and v_cache");
     p.seg[p.nseg++] = head_segment(wv, 8, EPI_STORE, v_cache, cache_len * 128, 128, cache_len);
   }
-  return run_gemv<4096, 4096, 2, 3>("cb_qkv_rope", p, static_cast<cudaStream_t>(stream));
+  return run_gemv<4096>("cb_qkv_rope", p, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cb_proj_residual(const void* x, int K, const void* w, int N, const void* residual,
@@ -584,8 +615,8 @@ extern "C" int cb_proj_residual(const void* x, int K, const void* w, int N, cons
   p.x = static_cast<const uint16_t*>(x);
   p.seg[p.nseg++] = half_segment(w, N, K, EPI_RESIDUAL, out, residual);
   auto s = static_cast<cudaStream_t>(stream);
-  if (K == 4096) return run_gemv<4096, 4096, 2, 3>("cb_proj_residual", p, s);
-  if (K == 14336) return run_gemv<14336, 7168, 1, 3, true>("cb_proj_residual", p, s);
+  if (K == 4096) return run_gemv<4096>("cb_proj_residual", p, s);
+  if (K == 14336) return run_gemv<14336>("cb_proj_residual", p, s);
   return fail(kErrUnsupported, "cb_proj_residual: K=%d (supported: 4096, 14336)", K);
 }
 
@@ -610,7 +641,7 @@ static int gate_up_common(const char* what, const void* x, const void* norm_w, f
     CB_REQUIRE(w && aligned16(w), "%s: weight invalid", what);
     p.seg[p.nseg++] = half_segment(w, N, 4096, mode, out, aux);
   }
-  return run_gemv<4096, 4096, 2, 3>(what, p, static_cast<cudaStream_t>(stream));
+  return run_gemv<4096>(what, p, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cb_gate_up_swiglu(const void* x, const void* norm_w, float eps, const void* w_gate,
@@ -633,18 +664,15 @@ extern "C" int cb_up_mul(const void* x, const void* norm_w, float eps, const voi
 
 namespace cb {
 int prepare_gemv() {
-  int rc = configure_smem("gemv", gemv_kernel<4096, 4096, 2, 3, false>,
-                          GemvCfg<4096, 4096, 2, 3, false>::SMEM);
-  if (rc == kOk)
-    rc = configure_smem("gemv", gemv_kernel<14336, 7168, 1, 3, true>,
-                        GemvCfg<14336, 7168, 1, 3, true>::SMEM);
+  int rc = configure_smem("gemv", gemv_kernel<4096>, kMaxSmem);
+  if (rc == kOk) rc = configure_smem("gemv", gemv_kernel<14336>, kMaxSmem);
   return rc;
 }
 }  // namespace cb
 
 extern "C" int64_t cb_lm_head_workspace_bytes(int k) {
-  // candidates: values [SMs*k] fp32, then indices [SMs*k] int64
-  const int64_t n = int64_t(sm_count()) * k;
+  // candidates: values [CTAs*k] fp32, then indices [CTAs*k] int64
+  const int64_t n = int64_t(lm_head_grid()) * k;
   return ((n * 4 + 15) / 16) * 16 + n * 8;
 }
 
@@ -667,12 +695,12 @@ extern "C" int cb_lm_head_topk(const void* x, const void* norm_w, float eps, con
   p.k = k;
   p.row_offset = row_offset;
   p.logits = logits;
-  const int64_t n = int64_t(sm_count()) * k;
+  const int64_t n = int64_t(lm_head_grid()) * k;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.cand_values = reinterpret_cast<float*>(ws);
   p.cand_indices = reinterpret_cast<int64_t*>(ws + ((n * 4 + 15) / 16) * 16);
   p.ticket = ticket;
   p.out_values = out_values;
   p.out_indices = out_indices;
-  return run_gemv<4096, 4096, 2, 3>("cb_lm_head_topk", p, static_cast<cudaStream_t>(stream));
+  return run_gemv<4096>("cb_lm_head_topk", p, static_cast<cudaStream_t>(stream));
 }

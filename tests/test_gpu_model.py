@@ -160,8 +160,9 @@ def test_config0_parity_with_reference(cuda, hbm_engine, meta, golden):
             print("step {}: engine-vs-refCPU {} | refGPU-vs-refCPU {} | engine-vs-refGPU {}".format(
                 step, {k: round(v, 5) for k, v in e_c.items()}, {k: round(v, 5) for k, v in g_c.items()},
                 {k: round(v, 5) for k, v in e_g.items()}))
+            # the reference's own GPU-vs-CPU disagreement is the noise floor
             for stats in (e_c, e_g):
-                assert stats["cos"] > 0.9995
+                assert 1.0 - stats["cos"] <= 1.5 * (1.0 - g_c["cos"]) + 1e-4
                 assert stats["max"] <= 1.5 * g_c["max"] + 0.05
                 assert stats["rmse"] <= 1.5 * g_c["rmse"]
             top_engine = set(torch.topk(engine, 10).indices.tolist())
