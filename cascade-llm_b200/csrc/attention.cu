@@ -16,6 +16,8 @@
 // Rows of the history (< P0) are fetched before griddepcontrol.wait: they were
 // written by earlier steps. Rows >= P0 were written by this step's QKV
 // kernel and are fetched only after the wait.
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 #include "cascade_b200.h"
@@ -365,4 +367,75 @@ extern "C" int cb_attention(const void* q, const void* k_cache, const void* v_ca
   p.err = error_word();
   return launch("cb_attention", attention_kernel, dim3(splits, 8, M), dim3(kAttnThreads),
                 AttnSmem::BYTES, static_cast<cudaStream_t>(stream), p);
+}
+
+// ============================================================================
+// Allocation-free variant of cb_attention.
+//
+// Some callers cannot call cudaMalloc: a host framework that owns the whole
+// device-memory budget through its own pool and hands this library only the
+// tensors of a call, or a caller in a latency-critical loop where an
+// allocation would synchronise the device. For them the split-KV scratch
+// (per-split partials and the last-CTA tickets) lives in a fixed
+// file-scope device array instead of a caller workspace. Every GPU that
+// loads this library holds these bytes until the process exits.
+// ============================================================================
+namespace cb {
+
+constexpr size_t kNoAllocPartialBytes = size_t(4) << 20;  // 4 MiB of partials
+constexpr int kNoAllocMaxTokens = 256;                     // tickets for 256 tokens
+
+struct NoAllocScratch {
+  float partials[kNoAllocPartialBytes / sizeof(float)];
+  unsigned int tickets[kNoAllocMaxTokens * 8];
+};
+static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
+
+// Device address of g_noalloc_scratch per device ordinal. In host code the
+// symbol's name is only a host-side stand-in, so the address is fetched with
+// cudaGetSymbolAddress once per device, with that device current.
+static std::mutex g_noalloc_lock;
+static NoAllocScratch* g_noalloc_ptr[64] = {};
+
+static int noalloc_scratch(NoAllocScratch** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(kErrCuda, "cb_attention_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(kErrUnsupported, "cb_attention_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> guard(g_noalloc_lock);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(kErrCuda, "cb_attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<NoAllocScratch*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return kOk;
+}
+
+}  // namespace cb
+
+extern "C" int cb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                    int64_t cache_len, const int32_t* position, int M, int splits,
+                                    int chunk, void* out, void* stream) {
+  if (M < 1 || M > kNoAllocMaxTokens)
+    return fail(kErrInvalid, "cb_attention_noalloc: M=%d exceeds the fixed scratch (1..%d tokens)", M,
+                kNoAllocMaxTokens);
+  const int64_t need = cb_attention_workspace_bytes(M, splits);
+  if (splits < 1 || need > int64_t(kNoAllocPartialBytes))
+    return fail(kErrInvalid,
+                "cb_attention_noalloc: M=%d x splits=%d needs %lld bytes of partials; the fixed scratch "
+                "holds %lld",
+                M, splits, (long long)need, (long long)kNoAllocPartialBytes);
+  NoAllocScratch* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != kOk) return rc;
+  // The tickets must start at zero; clear this call's range (a memset, not an
+  // allocation) in case an earlier launch was cut short.
+  cudaError_t e = cudaMemsetAsync(scratch->tickets, 0, size_t(M) * 8 * sizeof(unsigned int),
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(kErrCuda, "cb_attention_noalloc: clearing tickets: %s", cudaGetErrorString(e));
+  return cb_attention(q, k_cache, v_cache, cache_len, position, M, splits, chunk, out, scratch->partials,
+                      scratch->tickets, stream);
 }

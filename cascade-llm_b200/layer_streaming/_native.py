@@ -50,6 +50,7 @@ _SIGNATURES = {
     "cb_topk_merge": (_I, [_P, _P, _I, _P, _P, _I, _I, _P, _P, _P]),
     "cb_attention_workspace_bytes": (_I64, [_I, _I]),
     "cb_attention": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _P, _P, _P, _P]),
+    "cb_attention_noalloc": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _P, _P]),
     "cb_memcpy_h2d_async": (_I, [_P, _P, _I64, _P]),
 }
 

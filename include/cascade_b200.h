@@ -147,6 +147,24 @@ int cb_attention(const void* q, const void* k_cache, const void* v_cache, int64_
                  const int32_t* position, int M, int splits, int chunk, void* out, void* workspace,
                  unsigned int* tickets, void* stream);
 
+/* Allocation-free variant of cb_attention, for callers that cannot allocate
+ * device memory (a host framework that owns the whole memory budget in its
+ * own pool, or a latency-critical loop where cudaMalloc would synchronise the
+ * device). No counterpart in the reference, which has no custom kernels.
+ * The split-KV scratch is a fixed 4 MiB + 8 KiB static device array that
+ * every GPU loading this library holds until exit, so the limits are
+ * 1 <= M <= 256 and cb_attention_workspace_bytes(M, splits) <= 4 MiB
+ * (e.g. one decode token with up to 252 splits); larger requests fail with
+ * CB_ERR_INVALID. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture. Each call clears its ticket range with a
+ * cudaMemsetAsync and calls no cudaMalloc/cudaFree. All calls share the
+ * scratch, so calls that overlap on the GPU (different streams) race.
+ * Arguments otherwise as cb_attention. */
+int cb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
+                         const int32_t* position, int M, int splits, int chunk, void* out,
+                         void* stream);
+
 /* ---------------------------------------------------------------- copies */
 
 /* Host -> device copy of `bytes` on `stream` (cudaMemcpyAsync). The H2D leg
