@@ -96,6 +96,11 @@ __device__ __forceinline__ void bulk_g2s_stream(void* smem_dst, const void* gmem
       "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned, multiple of
+// 16 bytes): no destination, no completion, no registers held.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

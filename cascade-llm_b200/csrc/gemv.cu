@@ -33,493 +33,59 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "gemv_device.cuh"
 #include "internal.h"
 #include "cascade_b200.h"
+
+// Two CTAs of 8 warps per SM, one batch of UB units in flight per warp.
+#define CB_GEMV_CTAS_PER_SM 2
+#define CB_GEMV_DEPTH 1
 
 namespace cb {
 
 // Every GEMV launch is two CTAs per SM (one full wave at <= 128 registers
 // per thread); the LM-head candidate workspace is sized by the same grid.
-static int gemv_grid() { return 2 * sm_count(); }
+static int gemv_grid() { return CB_GEMV_CTAS_PER_SM * sm_count(); }
 static int lm_head_grid() { return gemv_grid(); }
 
-enum EpiMode : int {
-  EPI_STORE = 0,     // out[oA] = bf16(a), out[oB] = bf16(b)
-  EPI_RESIDUAL = 1,  // out[o] = bf16(aux[o] + bf16(acc))
-  EPI_ROPE = 2,      // RoPE on the (d, d+64) pair, store
-  EPI_SILU = 3,      // out[o] = bf16(silu(bf16(acc)))
-  EPI_MUL = 4,       // out[o] = bf16(aux[o] * bf16(acc))
-  EPI_SWIGLU = 5,    // out[j] = bf16(bf16(silu(bf16(a))) * bf16(b))
-  EPI_TOPK = 6,      // fp32 logits of bf16(acc) -> running top-k
-};
-
-constexpr int kThreads = 256;
-constexpr int kTopkMax = 64;
-constexpr size_t kMaxSmem = 227 * 1024;
-
-struct Segment {
-  const uint16_t* a_base;  // weight row base of slab A rows
-  const uint16_t* b_base;  // weight row base of slab B rows
-  int units;               // pair units in this segment
-  int group;               // units per group; a tile never crosses a group
-  int group_stride;        // weight rows between the starts of two groups
-  int mode;                // EpiMode
-  uint16_t* out;           // bf16 output base
-  const uint16_t* aux;     // residual / silu(gate), same indexing as out
-  int64_t head_stride;     // output elements between groups
-  int64_t b_offset;        // output index of row B minus that of row A
-  int64_t pos_stride;      // output elements per position (cache writes), 0 otherwise
-  int64_t pos_limit;       // cache capacity in positions (cache writes)
-};
-
-struct GemvParams {
-  Segment seg[3];
-  int nseg;
-  int total_units;
-  const uint16_t* x;       // activation row [K] (this launch's token)
-  const uint16_t* norm_w;  // RMSNorm weight [K] or null
-  float eps;
-  const float* inv_freq;   // [64] RoPE inverse frequencies
-  const int32_t* pos;      // device position of token 0 of the step
-  int token;               // token index within the step (position = *pos + token)
-  // top-k (EPI_TOPK)
-  int k;
-  int64_t row_offset;
-  float* logits;           // optional fp32 logits, indexed by local row
-  float* cand_values;      // [gridDim.x * k]
-  int64_t* cand_indices;
-  unsigned int* ticket;    // zero-initialised, reset by the last CTA
-  float* out_values;       // [k]
-  int64_t* out_indices;
-  int* err;
-};
-
-__device__ __forceinline__ int64_t unit_row(const Segment& s, int j) {
-  return int64_t(j / s.group) * s.group_stride + (j % s.group);
-}
-
-__device__ __forceinline__ bool ranks_before(float va, int64_t ia, float vb, int64_t ib) {
-  return va > vb || (va == vb && ia < ib);
-}
-
-// Warp-cooperative exact top-k over n (value, index) pairs in shared memory.
-__device__ void warp_select_rows_idx(const float* vals, const int64_t* idx, int n, int k, float* out_v,
-                                     int64_t* out_i) {
-  const int lane = threadIdx.x & 31;
-  float pv = __int_as_float(0x7F800000);
-  int64_t pi = -1;
-  for (int r = 0; r < k; ++r) {
-    float bv = -__int_as_float(0x7F800000);
-    int64_t bi = INT64_MAX;
-    for (int c = lane; c < n; c += 32) {
-      const float v = vals[c];
-      const int64_t i = idx[c];
-      if (ranks_before(pv, pi, v, i) && ranks_before(v, i, bv, bi)) {
-        bv = v;
-        bi = i;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-      const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-      if (ranks_before(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (lane == 0) {
-      out_v[r] = bv;
-      out_i[r] = bi;
-    }
-    pv = bv;
-    pi = bi;
-  }
-}
-
-// Warp-cooperative exact top-k over a CTA's logits in shared memory:
-// entry i < na is row a0 + i, entry i >= na is row b0 + (i - na). Missing
-// entries (n < k) are written as (-inf, INT64_MAX).
-__device__ void warp_select_rows(const float* vals, int n, int na, int64_t a0, int64_t b0, int k,
-                                 float* out_v, int64_t* out_i) {
-  const int lane = threadIdx.x & 31;
-  float pv = __int_as_float(0x7F800000);
-  int64_t pi = -1;
-  for (int r = 0; r < k; ++r) {
-    float bv = -__int_as_float(0x7F800000);
-    int64_t bi = INT64_MAX;
-    for (int c = lane; c < n; c += 32) {
-      const float v = vals[c];
-      const int64_t i = c < na ? a0 + c : b0 + (c - na);
-      if (ranks_before(pv, pi, v, i) && ranks_before(v, i, bv, bi)) {
-        bv = v;
-        bi = i;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-      const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-      if (ranks_before(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (lane == 0) {
-      out_v[r] = bv;
-      out_i[r] = bi;
-    }
-    pv = bv;
-    pi = bi;
-  }
-}
-
-// Warp-cooperative exact top-k of n candidates; lane 0 writes the result.
-// Round r selects the best candidate that ranks strictly after round r-1's.
-__device__ void warp_select_topk(const float* vals, const int64_t* idx, int n, int k,
-                                 float* out_v, int64_t* out_i) {
-  const int lane = threadIdx.x & 31;
-  float pv = __int_as_float(0x7F800000);  // +inf: everything ranks after it
-  int64_t pi = -1;
-  for (int r = 0; r < k; ++r) {
-    float bv = -__int_as_float(0x7F800000);
-    int64_t bi = INT64_MAX;
-    bool have = false;
-    for (int c = lane; c < n; c += 32) {
-      // candidates were written by other CTAs: read through L2
-      float v = __ldcg(vals + c);
-      int64_t i = __ldcg(reinterpret_cast<const long long*>(idx) + c);
-      if (ranks_before(pv, pi, v, i) && (!have || ranks_before(v, i, bv, bi))) {
-        bv = v;
-        bi = i;
-        have = true;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-      int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-      if (ranks_before(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (lane == 0) {
-      out_v[r] = bv;
-      out_i[r] = bi;
-    }
-    pv = bv;
-    pi = bi;
-  }
-}
-
-// Exact top-k of G sorted per-CTA candidate lists (k each, in global
-// memory), by the whole CTA. The k-th best of the union is at least the
-// largest per-list k-th value, so only candidates at or above that
-// threshold can qualify: one parallel pass finds the threshold, a second
-// copies the survivors to shared memory, and warp 0 selects among them.
-// `scratch` must hold kMergeCap floats + kMergeCap int64s.
-constexpr int kMergeCap = 1024;
-__device__ void block_merge_topk(const float* vals, const int64_t* idx, int G, int k, float* out_v,
-                                 int64_t* out_i, float* red, float* scratch) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float thr = -__int_as_float(0x7F800000);
-  for (int c = tid; c < G; c += blockDim.x) thr = fmaxf(thr, __ldcg(vals + size_t(c) * k + (k - 1)));
-  thr = warp_max(thr);
-  __syncthreads();
-  if (lane == 0) red[warp] = thr;
-  int* count = reinterpret_cast<int*>(red + 14);
-  if (tid == 0) *count = 0;
-  __syncthreads();
-  thr = red[0];
-  for (int q = 1; q < int(blockDim.x >> 5); ++q) thr = fmaxf(thr, red[q]);
-  float* sv = scratch;
-  int64_t* si = reinterpret_cast<int64_t*>(scratch + kMergeCap);
-  const int n = G * k;
-  for (int c = tid; c < n; c += blockDim.x) {
-    const float v = __ldcg(vals + c);
-    if (v >= thr) {
-      const int slot = atomicAdd(count, 1);
-      if (slot < kMergeCap) {
-        sv[slot] = v;
-        si[slot] = __ldcg(reinterpret_cast<const long long*>(idx) + c);
-      }
-    }
-  }
-  __syncthreads();
-  const int kept = *count;
-  if (warp == 0) {
-    if (kept <= kMergeCap)
-      warp_select_rows_idx(sv, si, kept, k, out_v, out_i);
-    else  // pathological ties: fall back to scanning every candidate
-      warp_select_topk(vals, idx, n, k, out_v, out_i);
-  }
-}
-
-
-}  // namespace cb
-
-namespace cb {
-
-__device__ __forceinline__ uint4 normalize8(uint4 xu, uint4 wu, float inv) {
-  const uint32_t in[4] = {xu.x, xu.y, xu.z, xu.w};
-  const uint32_t wv[4] = {wu.x, wu.y, wu.z, wu.w};
-  uint32_t out[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    // llama31.py:21-25: bf16(x * rsqrt(...)), then bf16(w * that)
-    const float lo = rbf(bf16lo(wv[q]) * rbf(bf16lo(in[q]) * inv));
-    const float hi = rbf(bf16hi(wv[q]) * rbf(bf16hi(in[q]) * inv));
-    out[q] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
-  }
-  return make_uint4(out[0], out[1], out[2], out[3]);
-}
-
-// Loads of weights that are read exactly once: 128-bit, not cached in L1.
-__device__ __forceinline__ uint4 ld_stream(const uint16_t* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
-
-__device__ __forceinline__ float silu_bf16(float g) {
-  // torch's silu on a bf16 tensor: x / (1 + exp(-x)) in fp32, rounded
-  return rbf(g / (1.0f + expf(-g)));
-}
-
-__device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int j, float a, float b,
-                              int pos) {
-  int64_t oa = int64_t(j / sg.group) * sg.head_stride + (j % sg.group);
-  if (sg.pos_stride) {
-    if (pos < 0 || pos >= sg.pos_limit) {  // never write outside the cache
-      if (p.err) atomicExch(p.err, 103);
-      return;
-    }
-    oa += int64_t(pos) * sg.pos_stride;
-  }
-  const int64_t ob = oa + sg.b_offset;
-  switch (sg.mode) {
-    case EPI_STORE:
-      sg.out[oa] = f2bf(a);
-      sg.out[ob] = f2bf(b);
-      break;
-    case EPI_RESIDUAL:
-      sg.out[oa] = f2bf(bf16f(__ldcg(sg.aux + oa)) + rbf(a));
-      sg.out[ob] = f2bf(bf16f(__ldcg(sg.aux + ob)) + rbf(b));
-      break;
-    case EPI_ROPE: {
-      // transformers modeling_llama.py:124-168: cos/sin of (inv_freq * pos)
-      // in fp32, cast to bf16; q*cos + rotate_half(q)*sin in bf16.
-      const int d = j % sg.group;
-      const float freq = __ldg(p.inv_freq + d) * float(pos);
-      const float c = rbf(cosf(freq)), s = rbf(sinf(freq));
-      const float qa = rbf(a), qb = rbf(b);
-      sg.out[oa] = f2bf(rbf(qa * c) + rbf(-qb * s));
-      sg.out[ob] = f2bf(rbf(qb * c) + rbf(qa * s));
-      break;
-    }
-    case EPI_SILU:
-      sg.out[oa] = f2bf(silu_bf16(rbf(a)));
-      sg.out[ob] = f2bf(silu_bf16(rbf(b)));
-      break;
-    case EPI_MUL:
-      sg.out[oa] = f2bf(bf16f(__ldcg(sg.aux + oa)) * rbf(a));
-      sg.out[ob] = f2bf(bf16f(__ldcg(sg.aux + ob)) * rbf(b));
-      break;
-    case EPI_SWIGLU:
-      sg.out[oa] = f2bf(silu_bf16(rbf(a)) * rbf(b));
-      break;
-    default:
-      break;
-  }
-}
-
+// Stand-alone projection: prefetch the first weight batch, wait for the
+// previous kernel (programmatic dependent launch), then run.
 template <int K>
-struct GemvShape {
-  static constexpr int WARPS = kThreads / 32;
-  static constexpr int KS = K / WARPS;          // K-slice of each warp
-  static constexpr int CPL = KS / 256;          // 16-byte chunks per lane per row slice
-  static constexpr int UB = (16 / (2 * CPL)) > 0 ? 16 / (2 * CPL) : 1;  // units per batch
-  static constexpr size_t RED = 0;              // [16] fp32 (norm partials, flag)
-  static constexpr size_t SMEM = RED + 16 * 4;  // + per-unit partials (+ logits), sized at launch
-  static_assert(KS % 256 == 0, "each warp's K-slice must be whole 512-byte lane groups");
-};
-
-// CTA-cooperative split-K GEMV. A CTA owns a contiguous range of units (row
-// pairs); each of its 8 warps streams its own 1/8 of K for EVERY unit of the
-// range (UB units, i.e. 2*UB*CPL 128-bit loads per lane, in flight per
-// batch), so all warps carry the same load and stream until the end. Per
-// unit, each warp reduces its two partial dots with shuffles into shared
-// memory; after ONE barrier the epilogues of all units run in parallel, one
-// thread per unit. The activation slice of a warp stays in registers. The
-// first batch of weight loads is issued before griddepcontrol.wait.
-template <int K>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
-  using S = GemvShape<K>;
+__global__ void __launch_bounds__(kThreads, CB_GEMV_CTAS_PER_SM) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  float* red = reinterpret_cast<float*>(smem + S::RED);
-  float* part = reinterpret_cast<float*>(smem + S::SMEM);  // [units][2][WARPS]
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-  const int G = gridDim.x;
-  const int u0 = int(int64_t(p.total_units) * blockIdx.x / G);
-  const int u1 = int(int64_t(p.total_units) * (blockIdx.x + 1) / G);
-  const int units = u1 - u0;
-  float* lrow = part + size_t(units) * 2 * S::WARPS;  // EPI_TOPK: this CTA's logits
-  const int kbase = warp * S::KS + lane * 8;            // first element of this lane
-
-  auto locate = [&](int u, int& seg, int& j) {
-    seg = 0;
-    j = u;
-    while (seg + 1 < p.nseg && j >= p.seg[seg].units) {
-      j -= p.seg[seg].units;
-      ++seg;
-    }
-  };
-  auto row_ptrs = [&](int u, const uint16_t*& ra, const uint16_t*& rb) {
-    int seg, j;
-    locate(u, seg, j);
-    const Segment& sg = p.seg[seg];
-    const int64_t row = int64_t(j / sg.group) * sg.group_stride + (j % sg.group);
-    ra = sg.a_base + row * K + kbase;
-    rb = sg.b_base + row * K + kbase;
-  };
-  uint4 w[S::UB][2][S::CPL];
-  auto load_batch = [&](int ub) {
-#pragma unroll
-    for (int i = 0; i < S::UB; ++i) {
-      if (ub + i < u1) {
-        const uint16_t *ra, *rb;
-        row_ptrs(ub + i, ra, rb);
-#pragma unroll
-        for (int c = 0; c < S::CPL; ++c) {
-          w[i][0][c] = ld_stream(ra + c * 256);
-          w[i][1][c] = ld_stream(rb + c * 256);
-        }
-      }
-    }
-  };
-
-  // weights do not depend on the previous kernel: start streaming now
-  load_batch(u0);
-
+  GemvRegs<K, CB_GEMV_DEPTH> r;
+  gemv_prefetch<K, CB_GEMV_DEPTH>(p, blockIdx.x, gridDim.x, r);
   grid_dep_wait();  // the activation row comes from the previous kernel
-  if (tid == 0) grid_dep_launch();
-  float inv = 1.0f;
-  if (p.norm_w) {
-    float ss = 0.f;
-    for (int c = tid; c < K / 8; c += kThreads) {
-      const uint4 v = ld_cg_u4(p.x + c * 8);
-      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        ss = fmaf(bf16lo(w4[q]), bf16lo(w4[q]), ss);
-        ss = fmaf(bf16hi(w4[q]), bf16hi(w4[q]), ss);
-      }
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    float tot = 0.f;
-#pragma unroll
-    for (int q = 0; q < S::WARPS; ++q) tot += red[q];
-    inv = rsqrtf(tot * (1.0f / K) + p.eps);
-  }
-  uint4 xr[S::CPL];
-#pragma unroll
-  for (int c = 0; c < S::CPL; ++c) {
-    uint4 v = ld_cg_u4(p.x + kbase + c * 256);
-    if (p.norm_w) v = normalize8(v, __ldg(reinterpret_cast<const uint4*>(p.norm_w + kbase + c * 256)), inv);
-    xr[c] = v;
-  }
-
-  for (int ub = u0; ub < u1; ub += S::UB) {
-    if (ub != u0) load_batch(ub);
-#pragma unroll
-    for (int i = 0; i < S::UB; ++i) {
-      if (ub + i < u1) {
-        float a = 0.f, b = 0.f;
-#pragma unroll
-        for (int c = 0; c < S::CPL; ++c) {
-          a = dot8(w[i][0][c], xr[c], a);
-          b = dot8(w[i][1][c], xr[c], b);
-        }
-        a = warp_sum(a);
-        b = warp_sum(b);
-        if (lane == 0) {
-          part[((ub + i - u0) * 2 + 0) * S::WARPS + warp] = a;
-          part[((ub + i - u0) * 2 + 1) * S::WARPS + warp] = b;
-        }
-      }
-    }
-  }
-  __syncthreads();
-
-  const int pos = p.pos ? __ldcg(p.pos) + p.token : 0;
-  for (int i = tid; i < units; i += kThreads) {
-    float a = 0.f, b = 0.f;
-#pragma unroll
-    for (int q = 0; q < S::WARPS; ++q) {
-      a += part[(i * 2 + 0) * S::WARPS + q];
-      b += part[(i * 2 + 1) * S::WARPS + q];
-    }
-    int seg, j;
-    locate(u0 + i, seg, j);
-    const Segment& sg = p.seg[seg];
-    if (sg.mode == EPI_TOPK) {
-      const float la = rbf(a), lb = rbf(b);  // F.linear(...) is bf16, then .float()
-      const int64_t row = int64_t(j / sg.group) * sg.group_stride + (j % sg.group);
-      if (p.logits) {
-        p.logits[row] = la;
-        p.logits[row + sg.b_offset] = lb;
-      }
-      lrow[i] = la;
-      lrow[units + i] = lb;
-    } else {
-      gemv_epilogue(p, sg, j, a, b, pos);
-    }
-  }
-
-  if (p.cand_values == nullptr) return;
-  // ---------------- LM head: this CTA's exact top-k, then the last CTA merges
-  __syncthreads();
-  if (warp == 0) {
-    const int64_t half = p.seg[0].b_offset;
-    warp_select_rows(lrow, 2 * units, units, p.row_offset + u0, p.row_offset + half + u0, p.k,
-                     p.cand_values + size_t(blockIdx.x) * p.k, p.cand_indices + size_t(blockIdx.x) * p.k);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const unsigned int ticket = atomicAdd(p.ticket, 1u);
-    red[15] = __int_as_float(ticket == unsigned(G - 1) ? 1 : 0);
-  }
-  __syncthreads();
-  if (__float_as_int(red[15]) != 1) return;
-  __threadfence();
-  block_merge_topk(p.cand_values, p.cand_indices, G, p.k, p.out_values, p.out_indices, red,
-                   reinterpret_cast<float*>(lrow));
-  if (tid == 0) *p.ticket = 0u;
+  if (threadIdx.x == 0) grid_dep_launch();
+  gemv_run<K, CB_GEMV_DEPTH>(p, smem, blockIdx.x, gridDim.x, r);
 }
 
 }  // namespace cb
 
 // ====================================================================== host
+#define CB_REQUIRE(cond, ...)                             \
+  do {                                                    \
+    if (!(cond)) return fail(kErrInvalid, __VA_ARGS__);   \
+  } while (0)
+
 namespace cb {
 
 int32_t* error_word();
 
-template <int K>
-static int run_gemv(const char* what, GemvParams& p, cudaStream_t stream) {
-  using S = GemvShape<K>;
-  int rc = configure_smem(what, gemv_kernel<K>, kMaxSmem);
-  if (rc != kOk) return rc;
+int finish_params(GemvParams& p) {
   p.total_units = 0;
   for (int i = 0; i < p.nseg; ++i) p.total_units += p.seg[i].units;
-  if (p.total_units == 0) return kOk;
   p.err = error_word();
+  return kOk;
+}
+
+template <int K>
+static int run_gemv(const char* what, GemvParams& p, cudaStream_t stream) {
+  using S = GemvShape<K, CB_GEMV_DEPTH>;
+  int rc = configure_smem(what, gemv_kernel<K>, kMaxSmem);
+  if (rc != kOk) return rc;
+  finish_params(p);
+  if (p.total_units == 0) return kOk;
   const int grid = gemv_grid();
   const size_t per_cta = size_t((p.total_units + grid - 1) / grid);
   size_t smem = S::SMEM + per_cta * 2 * S::WARPS * sizeof(float);  // per-unit partials
@@ -529,6 +95,14 @@ static int run_gemv(const char* what, GemvParams& p, cudaStream_t stream) {
   }
   if (smem > kMaxSmem) return fail(kErrInvalid, "%s: %zu units per CTA exceed shared memory", what, per_cta);
   return launch(what, gemv_kernel<K>, dim3(grid), dim3(kThreads), smem, stream, p);
+}
+
+int gemv_grid_size() { return gemv_grid(); }
+
+int prepare_gemv() {
+  int rc = configure_smem("gemv", gemv_kernel<4096>, kMaxSmem);
+  if (rc == kOk) rc = configure_smem("gemv", gemv_kernel<14336>, kMaxSmem);
+  return rc;
 }
 
 static Segment half_segment(const void* w, int N, int K, int mode, void* out, const void* aux) {
@@ -570,20 +144,16 @@ static Segment head_segment(const void* w, int heads, int mode, void* out, int64
 
 using namespace cb;
 
-#define CB_REQUIRE(cond, ...) \
-  do {                        \
-    if (!(cond)) return fail(kErrInvalid, __VA_ARGS__); \
-  } while (0)
+namespace cb {
 
-extern "C" int cb_qkv_rope(const void* x, const void* norm_w, float eps, const void* wq,
-                           const void* wk, const void* wv, const float* inv_freq,
-                           const int32_t* position, int token, void* q_out, void* k_cache,
-                           void* v_cache, int64_t cache_len, void* stream) {
+int build_qkv_params(GemvParams& p, const void* x, const void* norm_w, float eps, const void* wq,
+                     const void* wk, const void* wv, const float* inv_freq, const int32_t* position,
+                     int token, void* q_out, void* k_cache, void* v_cache, int64_t cache_len) {
   CB_REQUIRE(x && aligned16(x), "cb_qkv_rope: x must be a 16-byte aligned device pointer");
   CB_REQUIRE(!norm_w || aligned16(norm_w), "cb_qkv_rope: norm_w must be 16-byte aligned");
   CB_REQUIRE(inv_freq && position, "cb_qkv_rope: inv_freq and position are required");
   CB_REQUIRE(token >= 0, "cb_qkv_rope: token must be >= 0");
-  GemvParams p = {};
+  p = GemvParams{};
   p.x = static_cast<const uint16_t*>(x);
   p.norm_w = static_cast<const uint16_t*>(norm_w);
   p.eps = eps;
@@ -603,29 +173,26 @@ extern "C" int cb_qkv_rope(const void* x, const void* norm_w, float eps, const v
     CB_REQUIRE(aligned16(wv) && v_cache, "cb_qkv_rope: wv needs alignment and v_cache");
     p.seg[p.nseg++] = head_segment(wv, 8, EPI_STORE, v_cache, cache_len * 128, 128, cache_len);
   }
-  return run_gemv<4096>("cb_qkv_rope", p, static_cast<cudaStream_t>(stream));
+  return finish_params(p);
 }
 
-extern "C" int cb_proj_residual(const void* x, int K, const void* w, int N, const void* residual,
-                                void* out, void* stream) {
+int build_residual_params(GemvParams& p, const void* x, int K, const void* w, int N, const void* residual,
+                          void* out) {
   CB_REQUIRE(x && w && residual && out, "cb_proj_residual: null pointer");
   CB_REQUIRE(aligned16(x) && aligned16(w), "cb_proj_residual: x and w must be 16-byte aligned");
   CB_REQUIRE(N > 0 && N % 2 == 0, "cb_proj_residual: N must be even and positive");
-  GemvParams p = {};
+  CB_REQUIRE(K == 4096 || K == 14336, "cb_proj_residual: K=%d (supported: 4096, 14336)", K);
+  p = GemvParams{};
   p.x = static_cast<const uint16_t*>(x);
   p.seg[p.nseg++] = half_segment(w, N, K, EPI_RESIDUAL, out, residual);
-  auto s = static_cast<cudaStream_t>(stream);
-  if (K == 4096) return run_gemv<4096>("cb_proj_residual", p, s);
-  if (K == 14336) return run_gemv<14336>("cb_proj_residual", p, s);
-  return fail(kErrUnsupported, "cb_proj_residual: K=%d (supported: 4096, 14336)", K);
+  return finish_params(p);
 }
 
-static int gate_up_common(const char* what, const void* x, const void* norm_w, float eps,
-                          const void* w_gate, const void* w_up, int mode, void* out,
-                          const void* aux, void* stream) {
+int build_gate_up_params(GemvParams& p, const char* what, const void* x, const void* norm_w, float eps,
+                         const void* w_gate, const void* w_up, int mode, void* out, const void* aux) {
   CB_REQUIRE(x && out && aligned16(x), "%s: x/out invalid", what);
   CB_REQUIRE(!norm_w || aligned16(norm_w), "%s: norm_w must be 16-byte aligned", what);
-  GemvParams p = {};
+  p = GemvParams{};
   p.x = static_cast<const uint16_t*>(x);
   p.norm_w = static_cast<const uint16_t*>(norm_w);
   p.eps = eps;
@@ -641,6 +208,37 @@ static int gate_up_common(const char* what, const void* x, const void* norm_w, f
     CB_REQUIRE(w && aligned16(w), "%s: weight invalid", what);
     p.seg[p.nseg++] = half_segment(w, N, 4096, mode, out, aux);
   }
+  return finish_params(p);
+}
+
+}  // namespace cb
+
+extern "C" int cb_qkv_rope(const void* x, const void* norm_w, float eps, const void* wq,
+                           const void* wk, const void* wv, const float* inv_freq,
+                           const int32_t* position, int token, void* q_out, void* k_cache,
+                           void* v_cache, int64_t cache_len, void* stream) {
+  GemvParams p;
+  int rc = build_qkv_params(p, x, norm_w, eps, wq, wk, wv, inv_freq, position, token, q_out, k_cache, v_cache,
+                            cache_len);
+  if (rc != kOk) return rc;
+  return run_gemv<4096>("cb_qkv_rope", p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cb_proj_residual(const void* x, int K, const void* w, int N, const void* residual,
+                                void* out, void* stream) {
+  GemvParams p;
+  int rc = build_residual_params(p, x, K, w, N, residual, out);
+  if (rc != kOk) return rc;
+  auto s = static_cast<cudaStream_t>(stream);
+  return K == 4096 ? run_gemv<4096>("cb_proj_residual", p, s) : run_gemv<14336>("cb_proj_residual", p, s);
+}
+
+static int gate_up_common(const char* what, const void* x, const void* norm_w, float eps,
+                          const void* w_gate, const void* w_up, int mode, void* out,
+                          const void* aux, void* stream) {
+  GemvParams p;
+  int rc = build_gate_up_params(p, what, x, norm_w, eps, w_gate, w_up, mode, out, aux);
+  if (rc != kOk) return rc;
   return run_gemv<4096>(what, p, static_cast<cudaStream_t>(stream));
 }
 
@@ -661,14 +259,6 @@ extern "C" int cb_up_mul(const void* x, const void* norm_w, float eps, const voi
   return gate_up_common("cb_up_mul", x, norm_w, eps, nullptr, w_up, EPI_MUL, gate_act, gate_act,
                         stream);
 }
-
-namespace cb {
-int prepare_gemv() {
-  int rc = configure_smem("gemv", gemv_kernel<4096>, kMaxSmem);
-  if (rc == kOk) rc = configure_smem("gemv", gemv_kernel<14336>, kMaxSmem);
-  return rc;
-}
-}  // namespace cb
 
 extern "C" int64_t cb_lm_head_workspace_bytes(int k) {
   // candidates: values [CTAs*k] fp32, then indices [CTAs*k] int64

@@ -385,7 +385,6 @@ class Llama31DecodeExecutor:
                         self._unit(unit.layer_index, operation, runtime.unit_views(index), splits, chunk)
                 ops.position_advance(self.kv_cache.position, 1)
             self.kv_cache.length = saved
-            key = (id(runtime), bucket, self.kv_cache.generation, self._rows)
             self._graphs[key] = graph
         graph.replay()
         self.kv_cache.length += 1
