@@ -75,6 +75,9 @@ def parse_args():
                              "(for `ncu --profile-from-start off`) and exit")
     parser.add_argument("--micro", choices=sorted(MICRO_BYTES),
                         help="time one kernel alone on a small footprint (rotating copies > L2)")
+    parser.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
+                        help="N>1: tensor-parallel exchange through peer memory inside the projection "
+                             "kernels (default) or NCCL collectives between kernels")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -411,6 +414,137 @@ def reference_arm(args, rank):
     }
 
 
+def tensor_parallel(args, world, rank, local, device):
+    """N>1: one request decoded by all ranks (tensor parallelism over heads,
+    FFN rows and vocabulary), strong scaling of the same workload."""
+
+    import datetime
+
+    import torch.distributed as dist
+
+    from layer_streaming import ops
+    from layer_streaming.tensor_parallel import TensorParallelDecoder, TensorParallelWeights
+
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    weights = TensorParallelWeights.seeded(world, rank, device, seed=0)
+    extra = args.warmup + args.steps * 2 + 64
+    decoder = TensorParallelDecoder(Config(), weights, top_k=10, max_length=args.context + extra,
+                                    exchange=args.exchange)
+    ids = random_ids(args.context, seed=1).to(device)
+    with torch.inference_mode():
+        for start in range(0, args.context, 512):
+            state = decoder(ids[:, start:start + 512])
+    torch.cuda.synchronize(device)
+    decoder.check_errors()
+    token = state.topk_indices[..., 0].reshape(1, 1)
+
+    def barrier():
+        dist.barrier(device_ids=[local])
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            token = decoder(token).topk_indices[..., 0].reshape(1, 1)
+        torch.cuda.synchronize()
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            token = decoder(token).topk_indices[..., 0].reshape(1, 1)
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    clock_info = clocks.stop()
+    decoder.check_errors()
+    t = torch.tensor([start.elapsed_time(end) / args.steps], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+
+    # end to end: the token id from pinned host memory, the top-k read back
+    ids_host = torch.empty((1, 1), dtype=torch.int64).pin_memory()
+    ids_host[0, 0] = int(token.reshape(-1)[0])
+    with torch.inference_mode():
+        torch.cuda.synchronize()
+        barrier()
+        started = time.perf_counter()
+        for _ in range(args.steps):
+            state = decoder(ids_host)
+            values = state.topk_values.cpu()
+            indices = state.topk_indices.cpu()
+            ids_host[0, 0] = int(indices.reshape(-1)[0])
+        e2e_ms = (time.perf_counter() - started) * 1000.0 / args.steps
+    t = torch.tensor([e2e_ms], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e = {"value": round(float(t.item()), 4), "unit": "ms/token", "h2d_bytes_per_step": 8,
+           "d2h_bytes_per_step": values.numel() * 4 + indices.numel() * 8}
+
+    # dominant kernel on this rank: the gate+up GEMV over its FFN rows
+    x, out = decoder._x[0], decoder._mlp[0]
+    mats = [(weights["model.layers.{}.mlp.gate_proj.weight".format(i)],
+             weights["model.layers.{}.mlp.up_proj.weight".format(i)],
+             weights["model.layers.{}.post_attention_layernorm.weight".format(i)]) for i in range(32)]
+    for wg, wu, norm in mats:
+        ops.gate_up_swiglu(x, norm, 1e-5, wg, wu, out)
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(4):
+        for wg, wu, norm in mats:
+            ops.gate_up_swiglu(x, norm, 1e-5, wg, wu, out)
+    end.record(stream)
+    end.synchronize()
+    gate_up_ms = start.elapsed_time(end) / (4 * len(mats))
+    gate_up_bytes = GATE_UP_BYTES // world
+    peak, peak_kind = measured_peak()
+    achieved = gate_up_bytes / (gate_up_ms / 1000.0) / 1e9
+    context = decoder.kv_cache.length - args.steps - 1
+    rank_bytes = (LAYER_BYTES + HEAD_BYTES) // world + NORM_BYTES + (131_072 * (context + 1)) // world
+    rank_gbs = rank_bytes / (ms / 1000.0) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": round(ms, 4),
+        "unit": "ms/token",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, random token ids)",
+        "config": {
+            "workload": "llama31-8b decode bs=1, {}-token context".format(args.context),
+            "context": args.context,
+            "weights": "hbm-resident shards (heads, FFN rows, vocabulary)",
+            "flush": "none needed: per-rank weights ({:.1f} GB) larger than L2 (126 MB)".format(
+                weights.nbytes / 1e9),
+            "parallelism": "tp{} ({} exchange)".format(world, args.exchange),
+        },
+        "tokens_per_s": round(1000.0 / ms, 2),
+        "e2e": e2e,
+        "roofline": {
+            "bound": "hbm", "kernel": "gemv gate_up_swiglu shard (K=4096, N=2x{})".format(14336 // world),
+            "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": None,
+            "ms_per_launch": round(gate_up_ms, 5), "bytes_per_launch": gate_up_bytes,
+        },
+        "step_roofline": {
+            "achieved_per_rank": round(rank_gbs, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(rank_gbs / peak, 4), "bytes_per_token_per_rank": rank_bytes,
+        },
+        "cpu_baseline": None,
+        "gpu_launches": (1 + 32 * 5 + 1 + 2) * args.steps if args.exchange == "peer" else None,
+        "clocks": clock_info,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    decoder.close()
+    barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -426,18 +560,12 @@ def main():
     if args.micro:
         micro(args, device)
         return
-    group = None
     if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
-        group = dist
+        tensor_parallel(args, world, rank, local, device)
+        return
 
     def barrier():
-        if group is not None:
-            group.barrier()
+        pass
 
     extra = args.warmup + args.steps * 2 + 64
     plan, store, resident, runtime, executor = build_engine(device, args.context, extra)
@@ -459,10 +587,6 @@ def main():
     ms, token = time_decode(executor, runtime, token, args.steps, args.warmup, barrier)
     clock_info = clocks.stop()
     executor.check_errors()
-    if group is not None:
-        t = torch.tensor([ms], device=device)
-        group.all_reduce(t, op=group.ReduceOp.MAX)
-        ms = float(t.item())
     e2e = time_e2e(executor, runtime, token, args.steps)
     gate_up_ms = time_gate_up(executor, runtime, plan)
     peak, peak_kind = measured_peak()
@@ -491,9 +615,9 @@ def main():
             "context": args.context,
             "weights": "hbm-resident, matrix_group plan, resident vocab",
             "flush": "none needed: weights (16 GB) larger than L2 (126 MB)",
-            "parallelism": "replicas" if world > 1 else "single GPU",
+            "parallelism": "single GPU",
         },
-        "tokens_per_s": round(1000.0 / ms * world, 2),
+        "tokens_per_s": round(1000.0 / ms, 2),
         "e2e": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in e2e.items()},
         "roofline": {
             "bound": "hbm", "kernel": "gemv gate_up_swiglu (K=4096, N=2x14336)",
@@ -509,11 +633,7 @@ def main():
         "gpu_launches": kernels_per_step * args.steps,
         "clocks": clock_info,
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if group is not None:
-        group.barrier()
-        group.destroy_process_group()
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

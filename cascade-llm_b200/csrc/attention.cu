@@ -138,8 +138,9 @@ extern "C" int64_t cb_attention_workspace_bytes(int M, int splits) {
 }
 
 extern "C" int cb_attention(const void* q, const void* k_cache, const void* v_cache,
-                            int64_t cache_len, const int32_t* position, int M, int splits, int chunk,
-                            void* out, void* workspace, unsigned int* tickets, void* stream) {
+                            int64_t cache_len, const int32_t* position, int M, int kv_heads, int splits,
+                            int chunk, void* out, void* workspace, unsigned int* tickets, void* stream) {
+  if (kv_heads < 1 || kv_heads > 8) return fail(kErrInvalid, "cb_attention: kv_heads=%d (1..8)", kv_heads);
   if (!q || !k_cache || !v_cache || !position || !out || !workspace || !tickets)
     return fail(kErrInvalid, "cb_attention: null pointer");
   if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(q))
@@ -157,16 +158,17 @@ extern "C" int cb_attention(const void* q, const void* k_cache, const void* v_ca
   p.cache_len = cache_len;
   p.pos = position;
   p.M = M;
+  p.kv_heads = kv_heads;
   p.splits = splits;
   p.chunk = chunk;
   p.out = static_cast<uint16_t*>(out);
-  const int64_t rows = int64_t(M) * 32 * splits;
+  const int64_t rows = int64_t(M) * kv_heads * kGroup * splits;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_ml = reinterpret_cast<float*>(ws + rows * kHeadDim * 4);
   p.tickets = tickets;
   p.err = error_word();
-  return launch("cb_attention", attention_kernel, dim3(splits, 8, M), dim3(kAttnThreads),
+  return launch("cb_attention", attention_kernel, dim3(splits, kv_heads, M), dim3(kAttnThreads),
                 AttnSmem::BYTES, static_cast<cudaStream_t>(stream), p);
 }
 
@@ -237,6 +239,6 @@ extern "C" int cb_attention_noalloc(const void* q, const void* k_cache, const vo
   cudaError_t e = cudaMemsetAsync(scratch->tickets, 0, size_t(M) * 8 * sizeof(unsigned int),
                                   static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(kErrCuda, "cb_attention_noalloc: clearing tickets: %s", cudaGetErrorString(e));
-  return cb_attention(q, k_cache, v_cache, cache_len, position, M, splits, chunk, out, scratch->partials,
+  return cb_attention(q, k_cache, v_cache, cache_len, position, M, 8, splits, chunk, out, scratch->partials,
                       scratch->tickets, stream);
 }

@@ -23,10 +23,11 @@ struct AttnParams {
   int64_t cache_len;
   const int32_t* pos;
   int M, splits, chunk;
-  uint16_t* out;             // [M][4096]
-  float* part_o;             // [M][32][splits][128]
-  float* part_ml;            // [M][32][splits][2]
-  unsigned int* tickets;     // [M][8]
+  int kv_heads;              // KV heads of this rank (8 / tensor-parallel ranks)
+  uint16_t* out;             // [M][kv_heads * 4 * 128]
+  float* part_o;             // [M][kv_heads * 4][splits][128]
+  float* part_ml;            // [M][kv_heads * 4][splits][2]
+  unsigned int* tickets;     // [M][kv_heads]
   int* err;
 };
 
@@ -59,7 +60,7 @@ __device__ __forceinline__ int attn_range(const AttnParams& p, int s, int m, int
 // This lane's 4 dims of the 4 query heads of KV head g (token m).
 __device__ __forceinline__ void attn_load_q(const AttnParams& p, int m, int g, float (&q)[kGroup][4]) {
   const int lane = threadIdx.x & 31;
-  const uint16_t* qrow = p.q + (int64_t(m) * 32 + g * kGroup) * kHeadDim + 4 * lane;
+  const uint16_t* qrow = p.q + (int64_t(m) * p.kv_heads * kGroup + g * kGroup) * kHeadDim + 4 * lane;
 #pragma unroll
   for (int h = 0; h < kGroup; ++h) {
     const uint2 u = __ldcg(reinterpret_cast<const uint2*>(qrow + h * kHeadDim));
@@ -176,7 +177,7 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, co
     const int h = e / kHeadDim, d = e % kHeadDim;
     const float v = red[(0 * kGroup + h) * kHeadDim + d] + red[(1 * kGroup + h) * kHeadDim + d] +
                     red[(2 * kGroup + h) * kHeadDim + d] + red[(3 * kGroup + h) * kHeadDim + d];
-    const int64_t row = (int64_t(m) * 32 + g * kGroup + h) * p.splits + s;
+    const int64_t row = (int64_t(m) * p.kv_heads * kGroup + g * kGroup + h) * p.splits + s;
     p.part_o[row * kHeadDim + d] = v;
     if (d == 0) {
       p.part_ml[row * 2] = m_run[h];
@@ -186,7 +187,7 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, co
   __threadfence();
   sync();
   if (tid == 0) {
-    const unsigned int ticket = atomicAdd(&p.tickets[m * 8 + g], 1u);
+    const unsigned int ticket = atomicAdd(&p.tickets[m * p.kv_heads + g], 1u);
     red[0] = __int_as_float(ticket == unsigned(p.splits - 1) ? 1 : 0);
   }
   sync();
@@ -213,7 +214,8 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, co
     sync();
     for (int i = tid; i < kGroup * nb; i += kAttnConsumers) {
       const int h = i / nb, j = i % nb;
-      st_m[h * 256 + j] = __ldcg(p.part_ml + ((int64_t(m) * 32 + g * kGroup + h) * p.splits + base + j) * 2);
+      st_m[h * 256 + j] =
+          __ldcg(p.part_ml + ((int64_t(m) * p.kv_heads * kGroup + g * kGroup + h) * p.splits + base + j) * 2);
     }
     sync();
     if (warp < kGroup) {  // warp h: new running max and rescale of the previous blocks
@@ -226,8 +228,9 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, co
         const float mj = st_m[warp * 256 + j];
         const float w = mj == -__int_as_float(0x7F800000) ? 0.f : expf(mj - mnew);
         st_w[warp * 256 + j] = w;
-        lsum = fmaf(w, __ldcg(p.part_ml + ((int64_t(m) * 32 + g * kGroup + warp) * p.splits + base + j) * 2 + 1),
-                    lsum);
+        lsum = fmaf(
+            w, __ldcg(p.part_ml + ((int64_t(m) * p.kv_heads * kGroup + g * kGroup + warp) * p.splits + base + j) * 2 + 1),
+            lsum);
       }
       lsum = warp_sum(lsum);
       if (lane == 0) {
@@ -243,7 +246,7 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, co
       const int e = q ? e1 : e0;
       const int h = e / kHeadDim, d = e % kHeadDim;
       acc[q] *= st_s[h];
-      const float* po = p.part_o + ((int64_t(m) * 32 + g * kGroup + h) * p.splits + base) * kHeadDim + d;
+      const float* po = p.part_o + ((int64_t(m) * p.kv_heads * kGroup + g * kGroup + h) * p.splits + base) * kHeadDim + d;
       float sum = 0.f;
 #pragma unroll 8
       for (int j = 0; j < nb; ++j) sum = fmaf(st_w[h * 256 + j], __ldcg(po + int64_t(j) * kHeadDim), sum);
@@ -255,9 +258,9 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, co
   for (int q = 0; q < 2; ++q) {
     const int e = q ? e1 : e0;
     const int h = e / kHeadDim, d = e % kHeadDim;
-    p.out[int64_t(m) * 4096 + (g * kGroup + h) * kHeadDim + d] = f2bf(acc[q] / st_l[h]);
+    p.out[int64_t(m) * p.kv_heads * kGroup * kHeadDim + (g * kGroup + h) * kHeadDim + d] = f2bf(acc[q] / st_l[h]);
   }
-  if (tid == 0) p.tickets[m * 8 + g] = 0u;
+  if (tid == 0) p.tickets[m * p.kv_heads + g] = 0u;
 }
 
 }  // namespace cb

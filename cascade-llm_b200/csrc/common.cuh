@@ -116,6 +116,32 @@ __device__ __forceinline__ void grid_dep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ------------------------------------------- flags between GPUs (system scope)
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Wait until the (wrapping) sequence number at *flag reaches `target`, for at
+// most `limit_ns` nanoseconds of wall clock and kSpinLimit x 16 polls,
+// whichever ends first. Returns false on time-out (the caller records it).
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t* flag, uint32_t target, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (kSpinLimit << 4); ++i) {
+    if (int32_t(ld_acquire_sys(flag) - target) >= 0) return true;
+    if ((i & 255u) == 255u && globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  return false;
+}
+
 // ------------------------------------------------------------ loads/stores
 // Activations written by an earlier kernel are read through L2 only (.cg):
 // with overlapping dependent launches no stale L1 line can be hit.

@@ -88,7 +88,7 @@ static int run_gemv(const char* what, GemvParams& p, cudaStream_t stream) {
   if (p.total_units == 0) return kOk;
   const int grid = gemv_grid();
   const size_t per_cta = size_t((p.total_units + grid - 1) / grid);
-  size_t smem = S::SMEM + per_cta * 2 * S::WARPS * sizeof(float);  // per-unit partials
+  size_t smem = S::SMEM + per_cta * 2 * S::WK * sizeof(float);  // per-unit partials
   if (p.cand_values) {
     // EPI_TOPK: the CTA's logits, later reused as the last CTA's merge scratch
     smem += std::max(per_cta * 2 * sizeof(float), size_t(kMergeCap) * (sizeof(float) + sizeof(int64_t)));
@@ -99,9 +99,40 @@ static int run_gemv(const char* what, GemvParams& p, cudaStream_t stream) {
 
 int gemv_grid_size() { return gemv_grid(); }
 
+// Row lengths with a kernel instance: the model's 4096 and 14336, and their
+// tensor-parallel shards (O: 4096/N, down: 14336/N for N = 2, 4, 8).
+#define CB_GEMV_KS(X) X(512) X(1024) X(1792) X(2048) X(3584) X(4096) X(7168) X(14336)
+
+static int run_gemv_any(const char* what, int K, GemvParams& p, cudaStream_t stream) {
+  switch (K) {
+#define CB_CASE(k) \
+  case k:          \
+    return run_gemv<k>(what, p, stream);
+    CB_GEMV_KS(CB_CASE)
+#undef CB_CASE
+    default:
+      return fail(kErrUnsupported, "%s: K=%d has no kernel (512, 1024, 1792, 2048, 3584, 4096, 7168, 14336)",
+                  what, K);
+  }
+}
+
+static bool gemv_k_supported(int K) {
+  switch (K) {
+#define CB_CASE(k) case k:
+    CB_GEMV_KS(CB_CASE)
+#undef CB_CASE
+    return true;
+    default:
+      return false;
+  }
+}
+
 int prepare_gemv() {
-  int rc = configure_smem("gemv", gemv_kernel<4096>, kMaxSmem);
-  if (rc == kOk) rc = configure_smem("gemv", gemv_kernel<14336>, kMaxSmem);
+  int rc = kOk;
+#define CB_CASE(k) \
+  if (rc == kOk) rc = configure_smem("gemv", gemv_kernel<k>, kMaxSmem);
+  CB_GEMV_KS(CB_CASE)
+#undef CB_CASE
   return rc;
 }
 
@@ -148,7 +179,10 @@ namespace cb {
 
 int build_qkv_params(GemvParams& p, const void* x, const void* norm_w, float eps, const void* wq,
                      const void* wk, const void* wv, const float* inv_freq, const int32_t* position,
-                     int token, void* q_out, void* k_cache, void* v_cache, int64_t cache_len) {
+                     int token, void* q_out, void* k_cache, void* v_cache, int64_t cache_len, int q_heads,
+                     int kv_heads) {
+  CB_REQUIRE(q_heads >= 1 && q_heads <= 32 && kv_heads >= 1 && kv_heads <= 8,
+             "cb_qkv_rope: %d query / %d key-value heads (1..32 / 1..8)", q_heads, kv_heads);
   CB_REQUIRE(x && aligned16(x), "cb_qkv_rope: x must be a 16-byte aligned device pointer");
   CB_REQUIRE(!norm_w || aligned16(norm_w), "cb_qkv_rope: norm_w must be 16-byte aligned");
   CB_REQUIRE(inv_freq && position, "cb_qkv_rope: inv_freq and position are required");
@@ -162,16 +196,16 @@ int build_qkv_params(GemvParams& p, const void* x, const void* norm_w, float eps
   p.token = token;
   if (wq) {
     CB_REQUIRE(aligned16(wq) && q_out, "cb_qkv_rope: wq needs alignment and q_out");
-    p.seg[p.nseg++] = head_segment(wq, 32, EPI_ROPE, q_out, 128, 0);
+    p.seg[p.nseg++] = head_segment(wq, q_heads, EPI_ROPE, q_out, 128, 0);
   }
   if (wk || wv) CB_REQUIRE(cache_len > 0, "cb_qkv_rope: cache_len must be positive");
   if (wk) {
     CB_REQUIRE(aligned16(wk) && k_cache, "cb_qkv_rope: wk needs alignment and k_cache");
-    p.seg[p.nseg++] = head_segment(wk, 8, EPI_ROPE, k_cache, cache_len * 128, 128, cache_len);
+    p.seg[p.nseg++] = head_segment(wk, kv_heads, EPI_ROPE, k_cache, cache_len * 128, 128, cache_len);
   }
   if (wv) {
     CB_REQUIRE(aligned16(wv) && v_cache, "cb_qkv_rope: wv needs alignment and v_cache");
-    p.seg[p.nseg++] = head_segment(wv, 8, EPI_STORE, v_cache, cache_len * 128, 128, cache_len);
+    p.seg[p.nseg++] = head_segment(wv, kv_heads, EPI_STORE, v_cache, cache_len * 128, 128, cache_len);
   }
   return finish_params(p);
 }
@@ -181,22 +215,35 @@ int build_residual_params(GemvParams& p, const void* x, int K, const void* w, in
   CB_REQUIRE(x && w && residual && out, "cb_proj_residual: null pointer");
   CB_REQUIRE(aligned16(x) && aligned16(w), "cb_proj_residual: x and w must be 16-byte aligned");
   CB_REQUIRE(N > 0 && N % 2 == 0, "cb_proj_residual: N must be even and positive");
-  CB_REQUIRE(K == 4096 || K == 14336, "cb_proj_residual: K=%d (supported: 4096, 14336)", K);
+  CB_REQUIRE(gemv_k_supported(K), "cb_proj_residual: K=%d has no kernel", K);
   p = GemvParams{};
   p.x = static_cast<const uint16_t*>(x);
   p.seg[p.nseg++] = half_segment(w, N, K, EPI_RESIDUAL, out, residual);
   return finish_params(p);
 }
 
+int build_partial_params(GemvParams& p, const void* x, int K, const void* w, int N, float* out) {
+  CB_REQUIRE(x && w && out, "cb_proj_partial: null pointer");
+  CB_REQUIRE(aligned16(x) && aligned16(w), "cb_proj_partial: x and w must be 16-byte aligned");
+  CB_REQUIRE(N > 0 && N % 2 == 0, "cb_proj_partial: N must be even and positive");
+  CB_REQUIRE(gemv_k_supported(K), "cb_proj_partial: K=%d has no kernel", K);
+  p = GemvParams{};
+  p.x = static_cast<const uint16_t*>(x);
+  Segment s = half_segment(w, N, K, EPI_PARTIAL, nullptr, nullptr);
+  s.outf = out;
+  p.seg[p.nseg++] = s;
+  return finish_params(p);
+}
+
 int build_gate_up_params(GemvParams& p, const char* what, const void* x, const void* norm_w, float eps,
-                         const void* w_gate, const void* w_up, int mode, void* out, const void* aux) {
+                         const void* w_gate, const void* w_up, int N, int mode, void* out, const void* aux) {
   CB_REQUIRE(x && out && aligned16(x), "%s: x/out invalid", what);
+  CB_REQUIRE(N > 0 && N % 2 == 0, "%s: rows=%d must be even and positive", what, N);
   CB_REQUIRE(!norm_w || aligned16(norm_w), "%s: norm_w must be 16-byte aligned", what);
   p = GemvParams{};
   p.x = static_cast<const uint16_t*>(x);
   p.norm_w = static_cast<const uint16_t*>(norm_w);
   p.eps = eps;
-  const int N = 14336;
   if (mode == EPI_SWIGLU) {
     CB_REQUIRE(w_gate && w_up && aligned16(w_gate) && aligned16(w_up), "%s: weights invalid", what);
     Segment s = half_segment(w_gate, 2 * N, 4096, EPI_SWIGLU, out, nullptr);
@@ -216,10 +263,10 @@ int build_gate_up_params(GemvParams& p, const char* what, const void* x, const v
 extern "C" int cb_qkv_rope(const void* x, const void* norm_w, float eps, const void* wq,
                            const void* wk, const void* wv, const float* inv_freq,
                            const int32_t* position, int token, void* q_out, void* k_cache,
-                           void* v_cache, int64_t cache_len, void* stream) {
+                           void* v_cache, int64_t cache_len, int q_heads, int kv_heads, void* stream) {
   GemvParams p;
   int rc = build_qkv_params(p, x, norm_w, eps, wq, wk, wv, inv_freq, position, token, q_out, k_cache, v_cache,
-                            cache_len);
+                            cache_len, q_heads, kv_heads);
   if (rc != kOk) return rc;
   return run_gemv<4096>("cb_qkv_rope", p, static_cast<cudaStream_t>(stream));
 }
@@ -229,35 +276,77 @@ extern "C" int cb_proj_residual(const void* x, int K, const void* w, int N, cons
   GemvParams p;
   int rc = build_residual_params(p, x, K, w, N, residual, out);
   if (rc != kOk) return rc;
-  auto s = static_cast<cudaStream_t>(stream);
-  return K == 4096 ? run_gemv<4096>("cb_proj_residual", p, s) : run_gemv<14336>("cb_proj_residual", p, s);
+  return run_gemv_any("cb_proj_residual", K, p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cb_proj_partial(const void* x, int K, const void* w, int N, float* out, void* stream) {
+  GemvParams p;
+  int rc = build_partial_params(p, x, K, w, N, out);
+  if (rc != kOk) return rc;
+  return run_gemv_any("cb_proj_partial", K, p, static_cast<cudaStream_t>(stream));
 }
 
 static int gate_up_common(const char* what, const void* x, const void* norm_w, float eps,
-                          const void* w_gate, const void* w_up, int mode, void* out,
+                          const void* w_gate, const void* w_up, int rows, int mode, void* out,
                           const void* aux, void* stream) {
   GemvParams p;
-  int rc = build_gate_up_params(p, what, x, norm_w, eps, w_gate, w_up, mode, out, aux);
+  int rc = build_gate_up_params(p, what, x, norm_w, eps, w_gate, w_up, rows, mode, out, aux);
   if (rc != kOk) return rc;
   return run_gemv<4096>(what, p, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cb_gate_up_swiglu(const void* x, const void* norm_w, float eps, const void* w_gate,
-                                 const void* w_up, void* out, void* stream) {
-  return gate_up_common("cb_gate_up_swiglu", x, norm_w, eps, w_gate, w_up, EPI_SWIGLU, out,
+                                 const void* w_up, int rows, void* out, void* stream) {
+  return gate_up_common("cb_gate_up_swiglu", x, norm_w, eps, w_gate, w_up, rows, EPI_SWIGLU, out,
                         nullptr, stream);
 }
 
 extern "C" int cb_gate_silu(const void* x, const void* norm_w, float eps, const void* w_gate,
                             void* out, void* stream) {
-  return gate_up_common("cb_gate_silu", x, norm_w, eps, w_gate, nullptr, EPI_SILU, out, nullptr,
+  return gate_up_common("cb_gate_silu", x, norm_w, eps, w_gate, nullptr, 14336, EPI_SILU, out, nullptr,
                         stream);
 }
 
 extern "C" int cb_up_mul(const void* x, const void* norm_w, float eps, const void* w_up,
                          void* gate_act, void* stream) {
-  return gate_up_common("cb_up_mul", x, norm_w, eps, nullptr, w_up, EPI_MUL, gate_act, gate_act,
+  return gate_up_common("cb_up_mul", x, norm_w, eps, nullptr, w_up, 14336, EPI_MUL, gate_act, gate_act,
                         stream);
+}
+
+// Tensor-parallel exchange arguments shared by the two exchange entry points.
+static int set_exchange(GemvParams& p, const char* what, void* const* exchange, int rank, int world, int slot,
+                        int slots, const int32_t* epoch) {
+  CB_REQUIRE(exchange && epoch, "%s: exchange and epoch are required", what);
+  CB_REQUIRE(world >= 1 && world <= kXchgMaxWorld && rank >= 0 && rank < world,
+             "%s: rank %d of world %d (world 1..%d)", what, rank, world, kXchgMaxWorld);
+  CB_REQUIRE(slots >= 2 && slots % 2 == 0 && slot >= 0 && slot < slots,
+             "%s: slot %d of %d (slots even, >= 2)", what, slot, slots);
+  CB_REQUIRE(gemv_grid() <= kXchgMaxCtas, "%s: grid of %d CTAs exceeds the exchange flags", what, gemv_grid());
+  for (int q = 0; q < world; ++q) {
+    CB_REQUIRE(exchange[q] && aligned16(exchange[q]), "%s: exchange buffer of rank %d invalid", what, q);
+    p.xchg[q] = static_cast<uint8_t*>(exchange[q]);
+  }
+  p.rank = rank;
+  p.world = world;
+  p.slot = slot;
+  p.slots = slots;
+  p.epoch = epoch;
+  return kOk;
+}
+
+extern "C" int64_t cb_exchange_bytes(void) { return int64_t(kXchgBytes); }
+
+extern "C" int cb_proj_allreduce_residual(const void* x, int K, const void* w, int N, const void* residual,
+                                          void* out, void* const* exchange, int rank, int world, int slot,
+                                          int slots, const int32_t* epoch, void* stream) {
+  GemvParams p;
+  int rc = build_residual_params(p, x, K, w, N, residual, out);
+  if (rc != kOk) return rc;
+  CB_REQUIRE(N <= kXchgWidth, "cb_proj_allreduce_residual: N=%d exceeds the exchange width %d", N, kXchgWidth);
+  p.seg[0].mode = EPI_EXCHANGE;
+  rc = set_exchange(p, "cb_proj_allreduce_residual", exchange, rank, world, slot, slots, epoch);
+  if (rc != kOk) return rc;
+  return run_gemv_any("cb_proj_allreduce_residual", K, p, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int64_t cb_lm_head_workspace_bytes(int k) {
@@ -266,17 +355,16 @@ extern "C" int64_t cb_lm_head_workspace_bytes(int k) {
   return ((n * 4 + 15) / 16) * 16 + n * 8;
 }
 
-extern "C" int cb_lm_head_topk(const void* x, const void* norm_w, float eps, const void* w,
-                               int64_t rows, int64_t row_offset, int k, float* logits,
-                               float* out_values, int64_t* out_indices, void* workspace,
-                               unsigned int* ticket, void* stream) {
+static int build_lm_head_params(GemvParams& p, const void* x, const void* norm_w, float eps, const void* w,
+                                int64_t rows, int64_t row_offset, int k, float* logits, float* out_values,
+                                int64_t* out_indices, void* workspace, unsigned int* ticket) {
   CB_REQUIRE(x && w && out_values && out_indices && workspace && ticket, "cb_lm_head_topk: null pointer");
   CB_REQUIRE(aligned16(x) && aligned16(w), "cb_lm_head_topk: x and w must be 16-byte aligned");
   CB_REQUIRE(!norm_w || aligned16(norm_w), "cb_lm_head_topk: norm_w must be 16-byte aligned");
   CB_REQUIRE(rows > 0 && rows % 2 == 0 && rows <= (int64_t(1) << 30),
              "cb_lm_head_topk: rows must be even, positive and < 2^30 (got %lld)", (long long)rows);
   CB_REQUIRE(k >= 1 && k <= kTopkMax && k <= rows, "cb_lm_head_topk: need 1 <= k <= min(64, rows)");
-  GemvParams p = {};
+  p = GemvParams{};
   p.x = static_cast<const uint16_t*>(x);
   p.norm_w = static_cast<const uint16_t*>(norm_w);
   p.eps = eps;
@@ -292,5 +380,30 @@ extern "C" int cb_lm_head_topk(const void* x, const void* norm_w, float eps, con
   p.ticket = ticket;
   p.out_values = out_values;
   p.out_indices = out_indices;
+  return kOk;
+}
+
+extern "C" int cb_lm_head_topk(const void* x, const void* norm_w, float eps, const void* w,
+                               int64_t rows, int64_t row_offset, int k, float* logits,
+                               float* out_values, int64_t* out_indices, void* workspace,
+                               unsigned int* ticket, void* stream) {
+  GemvParams p;
+  int rc = build_lm_head_params(p, x, norm_w, eps, w, rows, row_offset, k, logits, out_values, out_indices,
+                                workspace, ticket);
+  if (rc != kOk) return rc;
   return run_gemv<4096>("cb_lm_head_topk", p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cb_lm_head_topk_allgather(const void* x, const void* norm_w, float eps, const void* w,
+                                         int64_t rows, int64_t row_offset, int k, float* out_values,
+                                         int64_t* out_indices, void* workspace, unsigned int* ticket,
+                                         void* const* exchange, int rank, int world, int slot, int slots,
+                                         const int32_t* epoch, void* stream) {
+  GemvParams p;
+  int rc = build_lm_head_params(p, x, norm_w, eps, w, rows, row_offset, k, nullptr, out_values, out_indices,
+                                workspace, ticket);
+  if (rc != kOk) return rc;
+  rc = set_exchange(p, "cb_lm_head_topk_allgather", exchange, rank, world, slot, slots, epoch);
+  if (rc != kOk) return rc;
+  return run_gemv<4096>("cb_lm_head_topk_allgather", p, static_cast<cudaStream_t>(stream));
 }

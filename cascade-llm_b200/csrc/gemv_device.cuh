@@ -15,7 +15,42 @@ enum EpiMode : int {
   EPI_MUL = 4,       // out[o] = bf16(aux[o] * bf16(acc))
   EPI_SWIGLU = 5,    // out[j] = bf16(bf16(silu(bf16(a))) * bf16(b))
   EPI_TOPK = 6,      // fp32 logits of bf16(acc) -> running top-k
+  EPI_PARTIAL = 7,   // outf[o] = acc (fp32, unrounded: a tensor-parallel partial sum)
+  EPI_EXCHANGE = 8,  // acc pushed to every rank; out[o] = bf16(aux[o] + bf16(sum over ranks))
 };
+
+// Tensor-parallel exchange buffer of one rank (device memory that every rank
+// maps; the same layout on all ranks). Two parities (slot & 1) alternate so
+// that a rank can push the next exchange while a peer still reads the last.
+//   flags  uint32 [2][kXchgFlagRows][kXchgMaxWorld]  sequence numbers; row c
+//          is written by CTA c of each rank's projection, the last row by the
+//          LM-head candidate gather
+//   cand_v float  [2][kXchgMaxWorld * kTopkMax]       top-k candidates (rank-major,
+//   cand_i int64  [2][kXchgMaxWorld * kTopkMax]        k per rank)
+//   data   float  [2][kXchgMaxWorld][kXchgWidth]      fp32 projection partials
+constexpr int kXchgMaxWorld = 8;
+constexpr int kXchgMaxCtas = 512;
+constexpr int kXchgFlagRows = kXchgMaxCtas + 1;
+constexpr int kXchgWidth = 4096;
+constexpr size_t kXchgFlags = 0;
+constexpr size_t kXchgCandV = ((size_t(2) * kXchgFlagRows * kXchgMaxWorld * 4 + 255) / 256) * 256;
+constexpr size_t kXchgCandI = kXchgCandV + size_t(2) * kXchgMaxWorld * 64 * 4;
+constexpr size_t kXchgData = kXchgCandI + size_t(2) * kXchgMaxWorld * 64 * 8;
+constexpr size_t kXchgBytes = kXchgData + size_t(2) * kXchgMaxWorld * kXchgWidth * 4;
+constexpr uint64_t kXchgWaitNs = 2000000000ull;  // a peer that is 2 s late is reported, not awaited
+
+__device__ __forceinline__ uint32_t* xchg_flag(uint8_t* base, int par, int row, int rank) {
+  return reinterpret_cast<uint32_t*>(base + kXchgFlags) + (par * kXchgFlagRows + row) * kXchgMaxWorld + rank;
+}
+__device__ __forceinline__ float* xchg_data(uint8_t* base, int par, int rank) {
+  return reinterpret_cast<float*>(base + kXchgData) + (par * kXchgMaxWorld + rank) * kXchgWidth;
+}
+__device__ __forceinline__ float* xchg_cand_v(uint8_t* base, int par) {
+  return reinterpret_cast<float*>(base + kXchgCandV) + par * kXchgMaxWorld * 64;
+}
+__device__ __forceinline__ int64_t* xchg_cand_i(uint8_t* base, int par) {
+  return reinterpret_cast<int64_t*>(base + kXchgCandI) + par * kXchgMaxWorld * 64;
+}
 
 constexpr int kThreads = 256;
 constexpr int kTopkMax = 64;
@@ -34,6 +69,7 @@ struct Segment {
   int64_t b_offset;        // output index of row B minus that of row A
   int64_t pos_stride;      // output elements per position (cache writes), 0 otherwise
   int64_t pos_limit;       // cache capacity in positions (cache writes)
+  float* outf;             // fp32 output (EPI_PARTIAL)
 };
 
 struct GemvParams {
@@ -56,6 +92,13 @@ struct GemvParams {
   float* out_values;       // [k]
   int64_t* out_indices;
   int* err;
+  // tensor-parallel exchange (EPI_EXCHANGE, and the LM head's candidate
+  // gather when world > 0): exchange buffer of every rank, this rank's own at
+  // [rank]; sequence number of this launch = epoch * slots + slot + 1
+  uint8_t* xchg[kXchgMaxWorld];
+  int rank, world;
+  int slot, slots;
+  const int32_t* epoch;    // device step counter, advanced once per step
 };
 
 __device__ __forceinline__ int64_t unit_row(const Segment& s, int j) {
@@ -292,6 +335,23 @@ static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int
     case EPI_SWIGLU:
       sg.out[oa] = f2bf(silu_bf16(rbf(a)) * rbf(b));
       break;
+    case EPI_PARTIAL:
+      sg.outf[oa] = a;
+      sg.outf[ob] = b;
+      break;
+    case EPI_EXCHANGE: {
+      // this rank's partial, into every rank's buffer (peer stores over NVLink)
+      const int par = p.slot & 1;
+#pragma unroll
+      for (int q = 0; q < kXchgMaxWorld; ++q) {
+        if (q < p.world) {
+          float* d = xchg_data(p.xchg[q], par, p.rank);
+          d[oa] = a;
+          d[ob] = b;
+        }
+      }
+      break;
+    }
     default:
       break;
   }
@@ -303,16 +363,21 @@ static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int
 template <int K, int DEPTH = 1>
 struct GemvShape {
   static constexpr int WARPS = kThreads / 32;
-  static constexpr int KS = K / WARPS;          // K-slice of each warp
-  static constexpr int CPL = KS / 256;          // 16-byte chunks per lane per row slice
-  static constexpr int UB = DEPTH * ((16 / (2 * CPL)) > 0 ? 16 / (2 * CPL) : 1);  // units per batch
-  // K = 14336: each warp keeps its activation slice in shared memory (its
-  // 28 registers would otherwise crowd out the weight batch)
-  static constexpr bool XSMEM = K > 8192;
-  static constexpr size_t RED = 0;                                   // [16] fp32 (norm partials, flag)
-  static constexpr size_t XS = RED + 16 * 4;                         // [K] bf16 when XSMEM
-  static constexpr size_t SMEM = XS + (XSMEM ? size_t(K) * 2 : 0);   // + per-unit partials (+ logits)
-  static_assert(KS % 256 == 0, "each warp's K-slice must be whole 512-byte lane groups");
+  static constexpr int GROUPS = K / 256;        // 512-byte lane groups per row
+  // WK warps split K (the largest of 8, 4, 2, 1 dividing GROUPS); the CTA's
+  // WARPS / WK warp rows work on different units at the same time
+  static constexpr int WK = GROUPS % 8 == 0 ? 8 : GROUPS % 4 == 0 ? 4 : GROUPS % 2 == 0 ? 2 : 1;
+  static constexpr int UL = WARPS / WK;          // units in flight side by side
+  static constexpr int KS = K / WK;              // K-slice of each warp
+  static constexpr int CPL = KS / 256;           // 16-byte chunks per lane per row slice
+  static constexpr int UB = DEPTH * ((16 / (2 * CPL)) > 0 ? 16 / (2 * CPL) : 1);  // units per warp per batch
+  // long K-slices keep the activation slice in shared memory (7 chunks = 28
+  // registers would otherwise crowd out the weight batch); one region per warp
+  static constexpr bool XSMEM = CPL > 4;
+  static constexpr size_t RED = 0;                                         // [16] fp32 (norm partials, flag)
+  static constexpr size_t XS = RED + 16 * 4;                               // [WARPS][KS] bf16 when XSMEM
+  static constexpr size_t SMEM = XS + (XSMEM ? size_t(WARPS) * KS * 2 : 0);  // + per-unit partials (+ logits)
+  static_assert(K % 256 == 0 && KS % 256 == 0, "K must be whole 512-byte lane groups");
 };
 
 template <int K, int DEPTH = 1>
@@ -330,15 +395,15 @@ __device__ __forceinline__ void gemv_locate(const GemvParams& p, int u, int& seg
 }
 
 // Weight rows of unit u for this lane: row A and row B of the pair.
-template <int K>
+template <int K, int DEPTH = 1>
 __device__ __forceinline__ void gemv_rows(const GemvParams& p, int u, const uint16_t*& ra,
                                           const uint16_t*& rb) {
-  using S = GemvShape<K>;
+  using S = GemvShape<K, DEPTH>;
   int seg, j;
   gemv_locate(p, u, seg, j);
   const Segment& sg = p.seg[seg];
   const int64_t row = int64_t(j / sg.group) * sg.group_stride + (j % sg.group);
-  const int kbase = (threadIdx.x >> 5) * S::KS + (threadIdx.x & 31) * 8;
+  const int kbase = ((threadIdx.x >> 5) % S::WK) * S::KS + (threadIdx.x & 31) * 8;
   ra = sg.a_base + row * K + kbase;
   rb = sg.b_base + row * K + kbase;
 }
@@ -346,11 +411,13 @@ __device__ __forceinline__ void gemv_rows(const GemvParams& p, int u, const uint
 template <int K, int DEPTH = 1>
 __device__ __forceinline__ void gemv_load_batch(const GemvParams& p, int ub, int u1, GemvRegs<K, DEPTH>& r) {
   using S = GemvShape<K, DEPTH>;
+  const int ul = (threadIdx.x >> 5) / S::WK;
 #pragma unroll
   for (int i = 0; i < S::UB; ++i) {
-    if (ub + i < u1) {
+    const int u = ub + i * S::UL + ul;
+    if (u < u1) {
       const uint16_t *ra, *rb;
-      gemv_rows<K>(p, ub + i, ra, rb);
+      gemv_rows<K, DEPTH>(p, u, ra, rb);
 #pragma unroll
       for (int c = 0; c < S::CPL; ++c) {
         r.w[i][0][c] = ld_stream(ra + c * 256);
@@ -410,8 +477,9 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   int u0, u1;
   gemv_cta_units(p, cta, ncta, u0, u1);
   const int units = u1 - u0;
-  float* lrow = part + size_t(units) * 2 * S::WARPS;  // EPI_TOPK: this CTA's logits
-  const int kbase = warp * S::KS + lane * 8;
+  float* lrow = part + size_t(units) * 2 * S::WK;  // EPI_TOPK: this CTA's logits
+  const int kp = warp % S::WK, ul = warp / S::WK;  // K-part and unit lane of this warp
+  const int kbase = kp * S::KS + lane * 8;
 
   float inv = 1.0f;
   if (p.norm_w) {
@@ -436,7 +504,7 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   // this warp's activation slice: registers, or (XSMEM) its own region of
   // shared memory, written and read by the same warp only
   uint4 xr[S::XSMEM ? 1 : S::CPL];
-  uint4* xw = reinterpret_cast<uint4*>(smem + S::XS) + warp * (S::KS / 8) + lane;
+  uint4* xw = reinterpret_cast<uint4*>(smem + S::XS) + warp * (S::KS / 8) + lane;  // this warp's region
 #pragma unroll
   for (int c = 0; c < S::CPL; ++c) {
     uint4 v = ld_cg_u4(p.x + kbase + c * 256);
@@ -452,7 +520,8 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   auto consume = [&](const GemvRegs<K, DEPTH>& rr, int ub) {
 #pragma unroll
     for (int i = 0; i < S::UB; ++i) {
-      if (ub + i < u1) {
+      const int u = ub + i * S::UL + ul;
+      if (u < u1) {
         float a = 0.f, b = 0.f;
 #pragma unroll
         for (int c = 0; c < S::CPL; ++c) {
@@ -463,13 +532,13 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
         a = warp_sum(a);
         b = warp_sum(b);
         if (lane == 0) {
-          part[((ub + i - u0) * 2 + 0) * S::WARPS + warp] = a;
-          part[((ub + i - u0) * 2 + 1) * S::WARPS + warp] = b;
+          part[((u - u0) * 2 + 0) * S::WK + kp] = a;
+          part[((u - u0) * 2 + 1) * S::WK + kp] = b;
         }
       }
     }
   };
-  for (int ub = u0; ub < u1; ub += S::UB) {
+  for (int ub = u0; ub < u1; ub += S::UB * S::UL) {
     if (ub != u0) gemv_load_batch<K, DEPTH>(p, ub, u1, r);
     consume(r, ub);
   }
@@ -479,9 +548,9 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   for (int i = tid; i < units; i += kThreads) {
     float a = 0.f, b = 0.f;
 #pragma unroll
-    for (int q = 0; q < S::WARPS; ++q) {
-      a += part[(i * 2 + 0) * S::WARPS + q];
-      b += part[(i * 2 + 1) * S::WARPS + q];
+    for (int q = 0; q < S::WK; ++q) {
+      a += part[(i * 2 + 0) * S::WK + q];
+      b += part[(i * 2 + 1) * S::WK + q];
     }
     int seg, j;
     gemv_locate(p, u0 + i, seg, j);
@@ -500,6 +569,44 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
     }
   }
 
+  if (p.world && p.cand_values == nullptr) {
+    // ---------------- tensor-parallel all-reduce of this CTA's rows. Every
+    // rank runs the same grid over the same units, so CTA `cta` of each rank
+    // owns the same output rows: signal the peers' CTA `cta`, wait for theirs,
+    // and sum the ranks' partials of these rows in rank order (the same bits
+    // on every rank).
+    __syncthreads();  // every partial of this CTA is stored
+    const int par = p.slot & 1;
+    const uint32_t seq = uint32_t(__ldcg(p.epoch)) * uint32_t(p.slots) + uint32_t(p.slot) + 1u;
+    if (tid < p.world) {
+      __threadfence_system();
+      st_release_sys(xchg_flag(p.xchg[tid], par, cta, p.rank), seq);
+      if (!wait_flag_sys(xchg_flag(p.xchg[p.rank], par, cta, tid), seq, kXchgWaitNs) && p.err)
+        atomicExch(p.err, 120);
+    }
+    __syncthreads();
+    uint8_t* own = p.xchg[p.rank];
+    for (int i = tid; i < units; i += kThreads) {
+      int seg, j;
+      gemv_locate(p, u0 + i, seg, j);
+      const Segment& sg = p.seg[seg];
+      const int64_t oa = int64_t(j / sg.group) * sg.head_stride + (j % sg.group);
+      const int64_t ob = oa + sg.b_offset;
+      float sa = 0.f, sb = 0.f;
+#pragma unroll
+      for (int q = 0; q < kXchgMaxWorld; ++q) {
+        if (q < p.world) {
+          const float* d = xchg_data(own, par, q);
+          sa += __ldcv(d + oa);
+          sb += __ldcv(d + ob);
+        }
+      }
+      // x + F.linear(...): the projection is rounded to bf16 once, then added
+      sg.out[oa] = f2bf(bf16f(__ldcg(sg.aux + oa)) + rbf(sa));
+      sg.out[ob] = f2bf(bf16f(__ldcg(sg.aux + ob)) + rbf(sb));
+    }
+    return;
+  }
   if (p.cand_values == nullptr) return;
   // ---------------- LM head: this CTA's exact top-k, then the last CTA merges
   __syncthreads();
@@ -519,17 +626,42 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   __threadfence();
   block_merge_topk(p.cand_values, p.cand_indices, ncta, p.k, p.out_values, p.out_indices, red, lrow);
   if (tid == 0) *p.ticket = 0u;
+  if (!p.world) return;
+  // ---------------- vocabulary-sharded LM head: gather every rank's k
+  // candidates (global row ids) into every rank's buffer, then merge.
+  __syncthreads();  // this rank's top-k is in out_values / out_indices
+  const int par = p.slot & 1;
+  const int k = p.k;
+  for (int e = tid; e < p.world * k; e += kThreads) {
+    const int q = e / k, i = e % k;
+    xchg_cand_v(p.xchg[q], par)[p.rank * k + i] = __ldcg(p.out_values + i);
+    xchg_cand_i(p.xchg[q], par)[p.rank * k + i] =
+        __ldcg(reinterpret_cast<const long long*>(p.out_indices) + i);
+  }
+  __syncthreads();
+  const uint32_t seq = uint32_t(__ldcg(p.epoch)) * uint32_t(p.slots) + uint32_t(p.slot) + 1u;
+  if (tid < p.world) {
+    __threadfence_system();
+    st_release_sys(xchg_flag(p.xchg[tid], par, kXchgMaxCtas, p.rank), seq);
+    if (!wait_flag_sys(xchg_flag(p.xchg[p.rank], par, kXchgMaxCtas, tid), seq, kXchgWaitNs) && p.err)
+      atomicExch(p.err, 121);
+  }
+  __syncthreads();
+  if (warp == 0)
+    warp_select_topk(xchg_cand_v(p.xchg[p.rank], par), xchg_cand_i(p.xchg[p.rank], par), p.world * k, k,
+                     p.out_values, p.out_indices);
 }
 
 // Host-side parameter builders (gemv.cu), shared with the decode-step table.
 int finish_params(GemvParams& p);
 int build_qkv_params(GemvParams& p, const void* x, const void* norm_w, float eps, const void* wq,
                      const void* wk, const void* wv, const float* inv_freq, const int32_t* position,
-                     int token, void* q_out, void* k_cache, void* v_cache, int64_t cache_len);
+                     int token, void* q_out, void* k_cache, void* v_cache, int64_t cache_len, int q_heads,
+                     int kv_heads);
 int build_residual_params(GemvParams& p, const void* x, int K, const void* w, int N, const void* residual,
                           void* out);
 int build_gate_up_params(GemvParams& p, const char* what, const void* x, const void* norm_w, float eps,
-                         const void* w_gate, const void* w_up, int mode, void* out, const void* aux);
+                         const void* w_gate, const void* w_up, int N, int mode, void* out, const void* aux);
 int gemv_grid_size();
 
 }  // namespace cb

@@ -184,6 +184,16 @@ __global__ void topk_merge_kernel(const float* av, const int64_t* ai, int na, co
   }
 }
 
+// ------------------------------------------------------------ residual
+// x + F.linear(...) when the projection's fp32 sum was assembled across
+// tensor-parallel ranks: out = bf16(x + bf16(sum)).
+__global__ void residual_add_kernel(const uint16_t* x, const float* sum, int n, uint16_t* out) {
+  grid_dep_wait();
+  if (threadIdx.x == 0) grid_dep_launch();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = f2bf(bf16f(__ldcg(x + i)) + rbf(__ldcg(sum + i)));
+}
+
 // ------------------------------------------------------------ position
 __global__ void position_kernel(int32_t* pos, const int64_t* src, int32_t value, int32_t add) {
   grid_dep_wait();
@@ -282,6 +292,13 @@ extern "C" int cb_topk_merge(const float* a_values, const int64_t* a_indices, in
   return launch("cb_topk_merge", topk_merge_kernel, dim3(1), dim3(32), 0,
                 static_cast<cudaStream_t>(stream), a_values, a_indices, na, b_values, b_indices, nb,
                 k, out_values, out_indices);
+}
+
+extern "C" int cb_residual_add_f32(const void* x, const float* sum, int n, void* out, void* stream) {
+  if (!x || !sum || !out || n < 1) return fail(kErrInvalid, "cb_residual_add_f32: bad arguments");
+  return launch("cb_residual_add_f32", residual_add_kernel, dim3((n + 255) / 256), dim3(256), 0,
+                static_cast<cudaStream_t>(stream), static_cast<const uint16_t*>(x), sum, n,
+                static_cast<uint16_t*>(out));
 }
 
 extern "C" int cb_position_set(int32_t* position, const int64_t* src, int32_t value, void* stream) {

@@ -25,6 +25,7 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _I64 = ctypes.c_int64
 _F = ctypes.c_float
+_PP = ctypes.POINTER(ctypes.c_void_p)
 
 _SIGNATURES = {
     "cb_version": (_I, []),
@@ -40,16 +41,28 @@ _SIGNATURES = {
     "cb_position_advance": (_I, [_P, ctypes.c_int32, _P]),
     "cb_embedding": (_I, [_P, _I, _P, _I64, _I, _P, _P]),
     "cb_rmsnorm": (_I, [_P, _P, _I, _I, _F, _P, _P]),
-    "cb_qkv_rope": (_I, [_P, _P, _F, _P, _P, _P, _P, _P, _I, _P, _P, _P, _I64, _P]),
+    "cb_qkv_rope": (_I, [_P, _P, _F, _P, _P, _P, _P, _P, _I, _P, _P, _P, _I64, _I, _I, _P]),
     "cb_proj_residual": (_I, [_P, _I, _P, _I, _P, _P, _P]),
-    "cb_gate_up_swiglu": (_I, [_P, _P, _F, _P, _P, _P, _P]),
+    "cb_proj_partial": (_I, [_P, _I, _P, _I, _P, _P]),
+    "cb_residual_add_f32": (_I, [_P, _P, _I, _P, _P]),
+    "cb_gate_up_swiglu": (_I, [_P, _P, _F, _P, _P, _I, _P, _P]),
     "cb_gate_silu": (_I, [_P, _P, _F, _P, _P, _P]),
     "cb_up_mul": (_I, [_P, _P, _F, _P, _P, _P]),
     "cb_lm_head_workspace_bytes": (_I64, [_I]),
     "cb_lm_head_topk": (_I, [_P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P, _P, _P, _P]),
     "cb_topk_merge": (_I, [_P, _P, _I, _P, _P, _I, _I, _P, _P, _P]),
+    "cb_exchange_bytes": (_I64, []),
+    "cb_exchange_alloc": (_I, [_PP]),
+    "cb_exchange_free": (_I, [_P]),
+    "cb_ipc_handle": (_I, [_P, _P]),
+    "cb_ipc_open": (_I, [_P, _PP]),
+    "cb_ipc_close": (_I, [_P]),
+    "cb_proj_allreduce_residual": (_I, [_P, _I, _P, _I, _P, _P, _PP, _I, _I, _I, _I, _P, _P]),
+    "cb_lm_head_topk_allgather": (
+        _I, [_P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P, _P, _PP, _I, _I, _I, _I, _P, _P]
+    ),
     "cb_attention_workspace_bytes": (_I64, [_I, _I]),
-    "cb_attention": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _P, _P, _P, _P]),
+    "cb_attention": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "cb_attention_noalloc": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _P, _P]),
     "cb_memcpy_h2d_async": (_I, [_P, _P, _I64, _P]),
 }

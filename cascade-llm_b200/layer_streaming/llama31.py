@@ -82,11 +82,11 @@ def llama3_inv_freq(config):
     return torch.where(medium, smoothed, scaled)
 
 
-def attention_split(tokens, length, sm_count):
+def attention_split(tokens, length, sm_count, kv_heads=8):
     """(splits, chunk) for the split-KV attention kernel: about two CTAs per
-    SM over (splits x 8 KV heads x tokens), chunks a multiple of 64 positions."""
+    SM over (splits x KV heads x tokens), chunks a multiple of 64 positions."""
 
-    target = max(1, (2 * sm_count) // (8 * tokens))
+    target = max(1, (2 * sm_count) // (kv_heads * tokens))
     per_split = -(-length // target)
     chunk = max(64, -(-per_split // 64) * 64)
     return -(-length // chunk), chunk

@@ -20,9 +20,11 @@ _SCHEMAS = {
     "qkv_rope": (
         "qkv_rope(Tensor x, Tensor? norm_w, float eps, Tensor? wq, Tensor? wk, Tensor? wv, "
         "Tensor inv_freq, Tensor position, int token, Tensor(a!)? q_out, Tensor(b!)? k_cache, "
-        "Tensor(c!)? v_cache) -> ()"
+        "Tensor(c!)? v_cache, int q_heads=32, int kv_heads=8) -> ()"
     ),
     "proj_residual": "proj_residual(Tensor x, Tensor w, Tensor residual, Tensor(a!) out) -> ()",
+    "proj_partial": "proj_partial(Tensor x, Tensor w, Tensor(a!) out) -> ()",
+    "residual_add_f32": "residual_add_f32(Tensor x, Tensor sum, Tensor(a!) out) -> ()",
     "gate_up_swiglu": (
         "gate_up_swiglu(Tensor x, Tensor? norm_w, float eps, Tensor w_gate, Tensor w_up, "
         "Tensor(a!) out) -> ()"
@@ -73,7 +75,8 @@ def rmsnorm(x, weight, eps, out):
     )
 
 
-def qkv_rope(x, norm_w, eps, wq, wk, wv, inv_freq, position, token, q_out, k_cache, v_cache):
+def qkv_rope(x, norm_w, eps, wq, wk, wv, inv_freq, position, token, q_out, k_cache, v_cache,
+             q_heads=32, kv_heads=8):
     cache = k_cache if k_cache is not None else v_cache
     cache_len = cache.shape[-2] if cache is not None else 0
     nat.check(
@@ -82,7 +85,7 @@ def qkv_rope(x, norm_w, eps, wq, wk, wv, inv_freq, position, token, q_out, k_cac
             nat.ptr(wq, BF16, "wq"), nat.ptr(wk, BF16, "wk"), nat.ptr(wv, BF16, "wv"),
             nat.ptr(inv_freq, torch.float32, "inv_freq"), nat.ptr(position, torch.int32, "position"),
             int(token), nat.ptr(q_out, BF16, "q_out"), nat.ptr(k_cache, BF16, "k_cache"),
-            nat.ptr(v_cache, BF16, "v_cache"), cache_len, _stream(x),
+            nat.ptr(v_cache, BF16, "v_cache"), cache_len, int(q_heads), int(kv_heads), _stream(x),
         ),
         "cascade.qkv_rope",
     )
@@ -98,11 +101,31 @@ def proj_residual(x, w, residual, out):
     )
 
 
+def proj_partial(x, w, out):
+    nat.check(
+        nat.lib().cb_proj_partial(
+            nat.ptr(x, BF16, "x"), w.shape[1], nat.ptr(w, BF16, "w"), w.shape[0],
+            nat.ptr(out, torch.float32, "out"), _stream(x),
+        ),
+        "cascade.proj_partial",
+    )
+
+
+def residual_add_f32(x, sum, out):
+    nat.check(
+        nat.lib().cb_residual_add_f32(
+            nat.ptr(x, BF16, "x"), nat.ptr(sum, torch.float32, "sum"), x.numel(), nat.ptr(out, BF16, "out"),
+            _stream(x),
+        ),
+        "cascade.residual_add_f32",
+    )
+
+
 def gate_up_swiglu(x, norm_w, eps, w_gate, w_up, out):
     nat.check(
         nat.lib().cb_gate_up_swiglu(
             nat.ptr(x, BF16, "x"), nat.ptr(norm_w, BF16, "norm_w"), float(eps),
-            nat.ptr(w_gate, BF16, "w_gate"), nat.ptr(w_up, BF16, "w_up"),
+            nat.ptr(w_gate, BF16, "w_gate"), nat.ptr(w_up, BF16, "w_up"), w_gate.shape[0],
             nat.ptr(out, BF16, "out"), _stream(x),
         ),
         "cascade.gate_up_swiglu",
@@ -165,13 +188,14 @@ def attention_workspace_bytes(m, splits):
 
 
 def attention(q, k_cache, v_cache, position, splits, chunk, out, workspace, tickets):
-    m = q.numel() // 4096
-    if tickets.numel() < 8 * m:
-        raise ValueError("attention needs 8 tickets per token")
+    kv_heads = k_cache.shape[-3]
+    m = q.numel() // (kv_heads * 512)
+    if tickets.numel() < kv_heads * m:
+        raise ValueError("attention needs one ticket per KV head and token")
     nat.check(
         nat.lib().cb_attention(
             nat.ptr(q, BF16, "q"), nat.ptr(k_cache, BF16, "k_cache"), nat.ptr(v_cache, BF16, "v_cache"),
-            k_cache.shape[-2], nat.ptr(position, torch.int32, "position"), m, int(splits), int(chunk),
+            k_cache.shape[-2], nat.ptr(position, torch.int32, "position"), m, kv_heads, int(splits), int(chunk),
             nat.ptr(out, BF16, "out"), nat.ptr(workspace, None, "workspace"),
             nat.ptr(tickets, torch.int32, "tickets"), _stream(q),
         ),

@@ -84,23 +84,34 @@ int cb_rmsnorm(const void* x, const void* w, int M, int hidden, float eps, void*
  * their output. x: hidden row [4096] of this token; norm_w: [4096] or NULL
  * (x already normalised); wq [4096,4096], wk/wv [1024,4096]; inv_freq: fp32
  * [64] (llama3-scaled); q_out: [4096] (this token's row); k_cache/v_cache:
- * this layer's [8, cache_len, 128]. */
+ * this layer's [kv_heads, cache_len, 128]. q_heads / kv_heads: 32 / 8, or a
+ * tensor-parallel rank's share (32/N, 8/N; the weights are that rank's rows). */
 int cb_qkv_rope(const void* x, const void* norm_w, float eps, const void* wq, const void* wk,
                 const void* wv, const float* inv_freq, const int32_t* position, int token,
-                void* q_out, void* k_cache, void* v_cache, int64_t cache_len, void* stream);
+                void* q_out, void* k_cache, void* v_cache, int64_t cache_len, int q_heads, int kv_heads,
+                void* stream);
 
 /* out = bf16(residual + bf16(x . W^T)) for one token row. Replaces the o_proj
  * (llama31.py:246-250) and down_proj (:272-280) F.linear + residual add.
  * K in {4096, 14336}; W: [N, K]; x: [K]; residual/out: [N] (may alias). */
 int cb_proj_residual(const void* x, int K, const void* w, int N, const void* residual, void* out,
                      void* stream);
+/* Tensor-parallel partial of the same projection: out[N] (fp32) = x . W^T
+ * over this rank's columns (K = 4096/N or 14336/N), unrounded, to be summed
+ * across ranks (all-reduce) and added with cb_residual_add_f32. Supported K:
+ * 512, 1024, 1792, 2048, 3584, 4096, 7168, 14336. */
+int cb_proj_partial(const void* x, int K, const void* w, int N, float* out, void* stream);
+/* out = bf16(x + bf16(sum)): the residual add of llama31.py:249/279 after a
+ * projection whose fp32 sum was all-reduced across ranks. x, out: [n] bf16. */
+int cb_residual_add_f32(const void* x, const float* sum, int n, void* out, void* stream);
 
 /* Post-attention RMSNorm + gate/up projection + SwiGLU for one token row:
  * out = bf16(bf16(silu(bf16(xn . Wg^T))) * bf16(xn . Wu^T)). Replaces
  * llama31.py:252-275 (the matrix_group `gate_up` unit). W_gate/W_up:
- * [14336, 4096]; out: [14336]. */
+ * [rows, 4096]; out: [rows]. rows = 14336, or a tensor-parallel rank's
+ * 14336/N (its rows of both matrices). */
 int cb_gate_up_swiglu(const void* x, const void* norm_w, float eps, const void* w_gate,
-                      const void* w_up, void* out, void* stream);
+                      const void* w_up, int rows, void* out, void* stream);
 /* The same split in two for the `matrix` granularity (gate_proj and up_proj
  * are separate units, llama31.py:252-271): cb_gate_silu writes
  * bf16(silu(...)), cb_up_mul multiplies it by the up projection in place. */
@@ -136,16 +147,17 @@ int cb_topk_merge(const float* a_values, const int64_t* a_indices, int na, const
  * llama31.py:182-234 (_repeat_kv + scaled_dot_product_attention): scale
  * 1/sqrt(128), fp32 softmax, bf16 output [M, 4096]. Split-KV: `splits`
  * chunks per (token, kv head), combined by the last CTA of each group.
- * q: [M, 32, 128]; k_cache/v_cache: this layer's [8, cache_len, 128].
+ * q: [M, 4*kv_heads, 128]; k_cache/v_cache: this layer's [kv_heads, cache_len, 128];
+ * kv_heads = 8, or a tensor-parallel rank's 8/N.
  * chunk = positions per split (multiple of 64); splits*chunk must cover the
  * longest context of the step. workspace: cb_attention_workspace_bytes(M,
  * splits) bytes of scratch for the per-split partials (no initialisation).
- * tickets: M*8 uint32 counters, zeroed once by the caller; each launch
+ * tickets: M*kv_heads uint32 counters, zeroed once by the caller; each launch
  * leaves them zero. */
 int64_t cb_attention_workspace_bytes(int M, int splits);
 int cb_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
-                 const int32_t* position, int M, int splits, int chunk, void* out, void* workspace,
-                 unsigned int* tickets, void* stream);
+                 const int32_t* position, int M, int kv_heads, int splits, int chunk, void* out,
+                 void* workspace, unsigned int* tickets, void* stream);
 
 /* Allocation-free variant of cb_attention, for callers that cannot allocate
  * device memory (a host framework that owns the whole memory budget in its
@@ -164,6 +176,53 @@ int cb_attention(const void* q, const void* k_cache, const void* v_cache, int64_
 int cb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
                          const int32_t* position, int M, int splits, int chunk, void* out,
                          void* stream);
+
+/* ------------------------------------------------------ tensor parallelism */
+
+/* Decode across N GPUs of one node (one process per GPU), an addition to the
+ * reference (whose executor is single-GPU, llama31.py:82-352): each rank
+ * holds query heads [32r/N, 32(r+1)/N), KV heads [8r/N, 8(r+1)/N), FFN rows
+ * [14336r/N, ...), the matching columns of o_proj / down_proj, and vocabulary
+ * rows [128256r/N, ...) of the LM head; the residual stream is replicated.
+ *
+ * Exchange buffer: cb_exchange_bytes() of device memory per rank, allocated
+ * zeroed by cb_exchange_alloc and mapped into the other ranks' processes with
+ * cb_ipc_handle (CB_IPC_HANDLE_BYTES opaque bytes, sent by any host channel)
+ * and cb_ipc_open. `exchange` arguments are HOST arrays of `world` device
+ * pointers: entry q is rank q's buffer as mapped in this process (entry
+ * `rank` is this rank's own).
+ *
+ * Sequence numbers: each launch of a step has a `slot` (0 <= slot < slots,
+ * slots even, the same on every rank); `epoch` is a device int32 step counter
+ * that every rank advances by one after each step (cb_position_advance).
+ * Ranks must issue the same launches in the same order. A peer that does not
+ * arrive within 2 s sets the error word (120: projection, 121: LM head) and
+ * the launch completes with undefined values instead of hanging. */
+#define CB_IPC_HANDLE_BYTES 64
+int64_t cb_exchange_bytes(void);
+int cb_exchange_alloc(void** buffer_out);
+int cb_exchange_free(void* buffer);
+int cb_ipc_handle(const void* buffer, void* handle_out);
+int cb_ipc_open(const void* handle, void** buffer_out);
+int cb_ipc_close(void* buffer);
+
+/* Row-parallel projection fused with its all-reduce and the residual add:
+ * out = bf16(residual + bf16(sum over ranks q of x_q . W_q^T)), where x_q / W_q
+ * are rank q's K columns (K = 4096/N for o_proj, 14336/N for down_proj) and
+ * the fp32 partials are summed in rank order, so every rank gets the same
+ * bits. Replaces F.linear + residual of llama31.py:246-250 / :276-280 under
+ * tensor parallelism. N <= 4096; residual may equal out. */
+int cb_proj_allreduce_residual(const void* x, int K, const void* w, int N, const void* residual, void* out,
+                               void* const* exchange, int rank, int world, int slot, int slots,
+                               const int32_t* epoch, void* stream);
+/* Vocabulary-sharded cb_lm_head_topk: this rank's `rows` rows starting at
+ * global row `row_offset`, its exact top-k, then the k candidates of every
+ * rank gathered through the exchange buffers and merged: every rank gets the
+ * global top-k (same tie rule). No full logits. */
+int cb_lm_head_topk_allgather(const void* x, const void* norm_w, float eps, const void* w, int64_t rows,
+                              int64_t row_offset, int k, float* out_values, int64_t* out_indices,
+                              void* workspace, unsigned int* ticket, void* const* exchange, int rank,
+                              int world, int slot, int slots, const int32_t* epoch, void* stream);
 
 /* ---------------------------------------------------------------- copies */
 

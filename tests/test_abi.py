@@ -42,9 +42,9 @@ def test_stream_key_matches_oracle():
 def test_invalid_arguments_fail_before_any_launch():
     handle = _native.load_library()
     # null pointers are rejected on the host: nothing reaches the GPU
-    assert handle.cb_qkv_rope(None, None, 1e-5, None, None, None, None, None, 0, None, None, None, 0, None) != 0
+    assert handle.cb_qkv_rope(None, None, 1e-5, None, None, None, None, None, 0, None, None, None, 0, 32, 8, None) != 0
     assert b"x must be" in handle.cb_last_error()
-    assert handle.cb_attention(None, None, None, 0, None, 1, 1, 64, None, None, None, None) != 0
+    assert handle.cb_attention(None, None, None, 0, None, 1, 8, 1, 64, None, None, None, None) != 0
     assert handle.cb_topk_merge(None, None, 0, None, None, 0, 10, None, None, None) != 0
     assert handle.cb_lm_head_topk(None, None, 0.0, None, 0, 0, 10, None, None, None, None, None, None) != 0
 

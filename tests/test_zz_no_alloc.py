@@ -31,7 +31,7 @@ def _reference(lib, q, kc, vc, pos, tokens, splits, chunk, stream):
     workspace = torch.empty(lib.cb_attention_workspace_bytes(tokens, splits), dtype=torch.uint8, device=q.device)
     tickets = torch.zeros(8 * tokens, dtype=torch.int32, device=q.device)
     rc = lib.cb_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), kc.shape[1], pos.data_ptr(), tokens,
-                          splits, chunk, out.data_ptr(), workspace.data_ptr(), tickets.data_ptr(), stream)
+                          8, splits, chunk, out.data_ptr(), workspace.data_ptr(), tickets.data_ptr(), stream)
     assert rc == 0, lib.cb_last_error()
     return out
 
