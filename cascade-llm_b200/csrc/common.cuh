@@ -1,7 +1,7 @@
 // Shared device helpers for the sm_100a kernels of the decode engine.
 //
 // Everything here is hand-written PTX or plain CUDA: BF16 bit conversions,
-// mbarrier + cp.async.bulk (TMA bulk copy, global -> shared, no multicast)
+// mbarrier + cp.async.bulk (TMA bulk copy, global -> this CTA's shared memory)
 // wrappers, and programmatic-dependent-launch controls (griddepcontrol).
 #pragma once
 
@@ -76,8 +76,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 
 // ------------------------------------------------- bulk copy (TMA, untiled)
 // Global -> shared::cta copy of `bytes` (multiple of 16, both addresses
-// 16-byte aligned) that completes `bytes` transactions on `bar`. No
-// multicast qualifier: every CTA fetches its own data.
+// 16-byte aligned) that completes `bytes` transactions on `bar`. Every CTA
+// fetches its own data into its own shared memory.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
                                          uint64_t* bar) {
   asm volatile(
