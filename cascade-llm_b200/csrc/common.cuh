@@ -122,24 +122,37 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// Tagged words: a 32-bit payload and the 32-bit sequence number of the
+// exchange that wrote it, stored as ONE aligned 64-bit word. A 64-bit scalar
+// access is single-copy atomic, so a reader that sees the expected tag sees
+// that exchange's payload: no fence or separate flag is needed, and each
+// reader waits for exactly the words it consumes.
+__device__ __forceinline__ uint64_t tag_word(uint32_t payload, uint32_t tag) {
+  return (uint64_t(tag) << 32) | payload;
+}
+__device__ __forceinline__ void st_tagged(uint64_t* p, uint64_t word) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(word) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_tagged(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Wait until the (wrapping) sequence number at *flag reaches `target`, for at
-// most `limit_ns` nanoseconds of wall clock and kSpinLimit x 16 polls,
-// whichever ends first. Returns false on time-out (the caller records it).
-__device__ __forceinline__ bool wait_flag_sys(const uint32_t* flag, uint32_t target, uint64_t limit_ns) {
+// Wait until the word at p carries `tag`, for at most `limit_ns` of wall
+// clock and kSpinLimit x 16 polls, whichever ends first; returns the payload
+// and sets *timed_out on time-out (the payload is then undefined).
+__device__ __forceinline__ uint32_t wait_tagged(const uint64_t* p, uint32_t tag, uint64_t limit_ns,
+                                                bool* timed_out) {
+  uint64_t w = ld_tagged(p);
+  if (uint32_t(w >> 32) == tag) return uint32_t(w);
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < (kSpinLimit << 4); ++i) {
-    if (int32_t(ld_acquire_sys(flag) - target) >= 0) return true;
-    if ((i & 255u) == 255u && globaltimer_ns() - t0 > limit_ns) return false;
+    w = ld_tagged(p);
+    if (uint32_t(w >> 32) == tag) return uint32_t(w);
+    if ((i & 255u) == 255u && globaltimer_ns() - t0 > limit_ns) break;
   }
-  return false;
+  *timed_out = true;
+  return uint32_t(w);
 }
 
 // ------------------------------------------------------------ loads/stores

@@ -321,7 +321,6 @@ static int set_exchange(GemvParams& p, const char* what, void* const* exchange, 
              "%s: rank %d of world %d (world 1..%d)", what, rank, world, kXchgMaxWorld);
   CB_REQUIRE(slots >= 2 && slots % 2 == 0 && slot >= 0 && slot < slots,
              "%s: slot %d of %d (slots even, >= 2)", what, slot, slots);
-  CB_REQUIRE(gemv_grid() <= kXchgMaxCtas, "%s: grid of %d CTAs exceeds the exchange flags", what, gemv_grid());
   for (int q = 0; q < world; ++q) {
     CB_REQUIRE(exchange[q] && aligned16(exchange[q]), "%s: exchange buffer of rank %d invalid", what, q);
     p.xchg[q] = static_cast<uint8_t*>(exchange[q]);
@@ -403,6 +402,8 @@ extern "C" int cb_lm_head_topk_allgather(const void* x, const void* norm_w, floa
   int rc = build_lm_head_params(p, x, norm_w, eps, w, rows, row_offset, k, nullptr, out_values, out_indices,
                                 workspace, ticket);
   if (rc != kOk) return rc;
+  CB_REQUIRE(row_offset >= 0 && row_offset + rows <= (int64_t(1) << 31),
+             "cb_lm_head_topk_allgather: global row ids must fit 31 bits");
   rc = set_exchange(p, "cb_lm_head_topk_allgather", exchange, rank, world, slot, slots, epoch);
   if (rc != kOk) return rc;
   return run_gemv<4096>("cb_lm_head_topk_allgather", p, static_cast<cudaStream_t>(stream));

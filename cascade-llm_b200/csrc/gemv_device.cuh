@@ -19,42 +19,38 @@ enum EpiMode : int {
   EPI_EXCHANGE = 8,  // acc pushed to every rank; out[o] = bf16(aux[o] + bf16(sum over ranks))
 };
 
-// Tensor-parallel exchange buffer of one rank (device memory that every rank
-// maps; the same layout on all ranks). Two parities (slot & 1) alternate so
-// that a rank can push the next exchange while a peer still reads the last.
-//   flags  uint32 [2][kXchgFlagRows][kXchgMaxWorld]  sequence numbers; row c
-//          is written by CTA c of each rank's projection, the last row by the
-//          LM-head candidate gather
-//   cand_v float  [2][kXchgMaxWorld * kTopkMax]       top-k candidates (rank-major,
-//   cand_i int64  [2][kXchgMaxWorld * kTopkMax]        k per rank)
-//   data   float  [2][kXchgMaxWorld][kXchgWidth]      fp32 projection partials
-constexpr int kXchgMaxWorld = 8;
-constexpr int kXchgMaxCtas = 512;
-constexpr int kXchgFlagRows = kXchgMaxCtas + 1;
-constexpr int kXchgWidth = 4096;
-constexpr size_t kXchgFlags = 0;
-constexpr size_t kXchgCandV = ((size_t(2) * kXchgFlagRows * kXchgMaxWorld * 4 + 255) / 256) * 256;
-constexpr size_t kXchgCandI = kXchgCandV + size_t(2) * kXchgMaxWorld * 64 * 4;
-constexpr size_t kXchgData = kXchgCandI + size_t(2) * kXchgMaxWorld * 64 * 8;
-constexpr size_t kXchgBytes = kXchgData + size_t(2) * kXchgMaxWorld * kXchgWidth * 4;
-constexpr uint64_t kXchgWaitNs = 2000000000ull;  // a peer that is 2 s late is reported, not awaited
-
-__device__ __forceinline__ uint32_t* xchg_flag(uint8_t* base, int par, int row, int rank) {
-  return reinterpret_cast<uint32_t*>(base + kXchgFlags) + (par * kXchgFlagRows + row) * kXchgMaxWorld + rank;
-}
-__device__ __forceinline__ float* xchg_data(uint8_t* base, int par, int rank) {
-  return reinterpret_cast<float*>(base + kXchgData) + (par * kXchgMaxWorld + rank) * kXchgWidth;
-}
-__device__ __forceinline__ float* xchg_cand_v(uint8_t* base, int par) {
-  return reinterpret_cast<float*>(base + kXchgCandV) + par * kXchgMaxWorld * 64;
-}
-__device__ __forceinline__ int64_t* xchg_cand_i(uint8_t* base, int par) {
-  return reinterpret_cast<int64_t*>(base + kXchgCandI) + par * kXchgMaxWorld * 64;
-}
-
 constexpr int kThreads = 256;
 constexpr int kTopkMax = 64;
 constexpr size_t kMaxSmem = 227 * 1024;
+
+// Tensor-parallel exchange buffer of one rank (device memory that every rank
+// maps; the same layout on all ranks). Every entry is a tagged 64-bit word
+// {payload, sequence number of the exchange} (common.cuh). Two parities
+// (slot & 1) alternate, so a rank can push the next exchange while a peer
+// still reads the last one.
+//   data   [2][kXchgMaxWorld][kXchgWidth]   fp32 projection partials, by source rank
+//   cand_v [2][kXchgMaxWorld * kTopkMax]    top-k candidate values (fp32), rank-major, k per rank
+//   cand_i [2][kXchgMaxWorld * kTopkMax]    their global row ids (uint32)
+constexpr int kXchgMaxWorld = 8;
+constexpr int kXchgWidth = 4096;
+constexpr size_t kXchgData = 0;
+constexpr size_t kXchgCandV = kXchgData + size_t(2) * kXchgMaxWorld * kXchgWidth * 8;
+constexpr size_t kXchgCandI = kXchgCandV + size_t(2) * kXchgMaxWorld * 64 * 8;
+constexpr size_t kXchgBytes = kXchgCandI + size_t(2) * kXchgMaxWorld * 64 * 8;
+constexpr uint64_t kXchgWaitNs = 2000000000ull;  // a peer that is 2 s late is reported, not awaited
+
+__device__ __forceinline__ uint64_t* xchg_data(uint8_t* base, int par, int rank) {
+  return reinterpret_cast<uint64_t*>(base + kXchgData) + (par * kXchgMaxWorld + rank) * kXchgWidth;
+}
+__device__ __forceinline__ uint64_t* xchg_cand_v(uint8_t* base, int par) {
+  return reinterpret_cast<uint64_t*>(base + kXchgCandV) + par * kXchgMaxWorld * 64;
+}
+__device__ __forceinline__ uint64_t* xchg_cand_i(uint8_t* base, int par) {
+  return reinterpret_cast<uint64_t*>(base + kXchgCandI) + par * kXchgMaxWorld * 64;
+}
+__device__ __forceinline__ uint32_t xchg_seq(const int32_t* epoch, int slots, int slot) {
+  return uint32_t(__ldcg(epoch)) * uint32_t(slots) + uint32_t(slot) + 1u;
+}
 
 struct Segment {
   const uint16_t* a_base;  // weight row base of slab A rows
@@ -340,16 +336,33 @@ static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int
       sg.outf[ob] = b;
       break;
     case EPI_EXCHANGE: {
-      // this rank's partial, into every rank's buffer (peer stores over NVLink)
+      // Push this rank's partials of rows oa / ob into every rank's buffer
+      // (peer stores over NVLink), then sum every rank's partials of the same
+      // rows in rank order, so all ranks compute the same bits, and add the
+      // residual: x + F.linear(...) rounds the projection to bf16 once.
       const int par = p.slot & 1;
+      const uint32_t seq = xchg_seq(p.epoch, p.slots, p.slot);
 #pragma unroll
       for (int q = 0; q < kXchgMaxWorld; ++q) {
         if (q < p.world) {
-          float* d = xchg_data(p.xchg[q], par, p.rank);
-          d[oa] = a;
-          d[ob] = b;
+          uint64_t* d = xchg_data(p.xchg[q], par, p.rank);
+          st_tagged(d + oa, tag_word(__float_as_uint(a), seq));
+          st_tagged(d + ob, tag_word(__float_as_uint(b), seq));
         }
       }
+      float sa = 0.f, sb = 0.f;
+      bool late = false;
+#pragma unroll
+      for (int q = 0; q < kXchgMaxWorld; ++q) {
+        if (q < p.world) {
+          const uint64_t* d = xchg_data(p.xchg[p.rank], par, q);
+          sa += __uint_as_float(wait_tagged(d + oa, seq, kXchgWaitNs, &late));
+          sb += __uint_as_float(wait_tagged(d + ob, seq, kXchgWaitNs, &late));
+        }
+      }
+      if (late && p.err) atomicExch(p.err, 120);
+      sg.out[oa] = f2bf(bf16f(__ldcg(sg.aux + oa)) + rbf(sa));
+      sg.out[ob] = f2bf(bf16f(__ldcg(sg.aux + ob)) + rbf(sb));
       break;
     }
     default:
@@ -569,44 +582,6 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
     }
   }
 
-  if (p.world && p.cand_values == nullptr) {
-    // ---------------- tensor-parallel all-reduce of this CTA's rows. Every
-    // rank runs the same grid over the same units, so CTA `cta` of each rank
-    // owns the same output rows: signal the peers' CTA `cta`, wait for theirs,
-    // and sum the ranks' partials of these rows in rank order (the same bits
-    // on every rank).
-    __syncthreads();  // every partial of this CTA is stored
-    const int par = p.slot & 1;
-    const uint32_t seq = uint32_t(__ldcg(p.epoch)) * uint32_t(p.slots) + uint32_t(p.slot) + 1u;
-    if (tid < p.world) {
-      __threadfence_system();
-      st_release_sys(xchg_flag(p.xchg[tid], par, cta, p.rank), seq);
-      if (!wait_flag_sys(xchg_flag(p.xchg[p.rank], par, cta, tid), seq, kXchgWaitNs) && p.err)
-        atomicExch(p.err, 120);
-    }
-    __syncthreads();
-    uint8_t* own = p.xchg[p.rank];
-    for (int i = tid; i < units; i += kThreads) {
-      int seg, j;
-      gemv_locate(p, u0 + i, seg, j);
-      const Segment& sg = p.seg[seg];
-      const int64_t oa = int64_t(j / sg.group) * sg.head_stride + (j % sg.group);
-      const int64_t ob = oa + sg.b_offset;
-      float sa = 0.f, sb = 0.f;
-#pragma unroll
-      for (int q = 0; q < kXchgMaxWorld; ++q) {
-        if (q < p.world) {
-          const float* d = xchg_data(own, par, q);
-          sa += __ldcv(d + oa);
-          sb += __ldcv(d + ob);
-        }
-      }
-      // x + F.linear(...): the projection is rounded to bf16 once, then added
-      sg.out[oa] = f2bf(bf16f(__ldcg(sg.aux + oa)) + rbf(sa));
-      sg.out[ob] = f2bf(bf16f(__ldcg(sg.aux + ob)) + rbf(sb));
-    }
-    return;
-  }
   if (p.cand_values == nullptr) return;
   // ---------------- LM head: this CTA's exact top-k, then the last CTA merges
   __syncthreads();
@@ -627,29 +602,31 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   block_merge_topk(p.cand_values, p.cand_indices, ncta, p.k, p.out_values, p.out_indices, red, lrow);
   if (tid == 0) *p.ticket = 0u;
   if (!p.world) return;
-  // ---------------- vocabulary-sharded LM head: gather every rank's k
-  // candidates (global row ids) into every rank's buffer, then merge.
+  // ---------------- vocabulary-sharded LM head: push this rank's k
+  // candidates (global row ids) into every rank's buffer, gather all ranks'
+  // candidates into shared memory and select the global top-k.
   __syncthreads();  // this rank's top-k is in out_values / out_indices
   const int par = p.slot & 1;
   const int k = p.k;
+  const uint32_t seq = xchg_seq(p.epoch, p.slots, p.slot);
   for (int e = tid; e < p.world * k; e += kThreads) {
     const int q = e / k, i = e % k;
-    xchg_cand_v(p.xchg[q], par)[p.rank * k + i] = __ldcg(p.out_values + i);
-    xchg_cand_i(p.xchg[q], par)[p.rank * k + i] =
-        __ldcg(reinterpret_cast<const long long*>(p.out_indices) + i);
+    const float v = __ldcg(p.out_values + i);
+    const uint32_t row = uint32_t(__ldcg(reinterpret_cast<const long long*>(p.out_indices) + i));
+    st_tagged(xchg_cand_v(p.xchg[q], par) + p.rank * k + i, tag_word(__float_as_uint(v), seq));
+    st_tagged(xchg_cand_i(p.xchg[q], par) + p.rank * k + i, tag_word(row, seq));
   }
-  __syncthreads();
-  const uint32_t seq = uint32_t(__ldcg(p.epoch)) * uint32_t(p.slots) + uint32_t(p.slot) + 1u;
-  if (tid < p.world) {
-    __threadfence_system();
-    st_release_sys(xchg_flag(p.xchg[tid], par, kXchgMaxCtas, p.rank), seq);
-    if (!wait_flag_sys(xchg_flag(p.xchg[p.rank], par, kXchgMaxCtas, tid), seq, kXchgWaitNs) && p.err)
-      atomicExch(p.err, 121);
+  float* sv = lrow;  // merge scratch: kMergeCap values, then kMergeCap int64 ids
+  int64_t* si = reinterpret_cast<int64_t*>(lrow + kMergeCap);
+  bool late = false;
+  uint8_t* own = p.xchg[p.rank];
+  for (int e = tid; e < p.world * k; e += kThreads) {
+    sv[e] = __uint_as_float(wait_tagged(xchg_cand_v(own, par) + e, seq, kXchgWaitNs, &late));
+    si[e] = int64_t(wait_tagged(xchg_cand_i(own, par) + e, seq, kXchgWaitNs, &late));
   }
+  if (late && p.err) atomicExch(p.err, 121);
   __syncthreads();
-  if (warp == 0)
-    warp_select_topk(xchg_cand_v(p.xchg[p.rank], par), xchg_cand_i(p.xchg[p.rank], par), p.world * k, k,
-                     p.out_values, p.out_indices);
+  if (warp == 0) warp_select_rows_idx(sv, si, p.world * k, k, p.out_values, p.out_indices);
 }
 
 // Host-side parameter builders (gemv.cu), shared with the decode-step table.

@@ -9,8 +9,9 @@ single-GPU kernels.
 Model level: the tensor-parallel decoder over a world of one reproduces the
 reference's golden run through both exchange paths, and
 over two GPUs (when the box has them, via torchrun of tests/tp_worker.py) it
-reproduces the same golden run through both exchange paths, with the same
-bits on every rank.
+meets the same top-k criteria against the golden run through both exchange
+paths (teacher-forced), decodes the golden greedy ids up to the first golden
+near-tie, and every rank holds the same bits.
 """
 
 import ctypes

@@ -3,13 +3,17 @@ from test_gpu_tensor_parallel.py; prints TP-PARITY-OK on rank 0 when every
 check passes).
 
 Each rank generates its shards of the seeded model (BASELINE config 0
-weights), decodes the 6-token seeded prompt + 8 greedy steps through the
-peer-memory exchange and through NCCL, and checks that
-  * all ranks hold the same top-k bits after every step,
-  * both exchange paths give the same greedy tokens and top-k values within
-    rtol/atol 2e-2,
-  * the greedy tokens and top-k values reproduce the reference's golden run
-    (tests/golden/config0.json) within the same tolerance.
+weights) and runs the golden run's 9 steps through the peer-memory exchange
+and through NCCL, checking that
+  * all ranks hold the same top-k bits after every step;
+  * fed the golden run's inputs (tests/golden/config0.json), every step's
+    top-k values are within rtol/atol 2e-2 of the reference's, with the same
+    ids wherever the neighbouring gaps exceed that tolerance (as the
+    single-GPU parity test checks);
+  * free-running greedy decoding gives the reference's ids until the first
+    step whose golden top-1 / top-2 gap lies inside the tolerance, where the
+    pick must be one of the tied candidates (a different fp32 summation order
+    may legitimately break such a tie the other way).
 """
 
 import datetime
@@ -43,6 +47,18 @@ class Config:
     }
 
 
+def run(decoder, device, inputs):
+    """One step per entry of `inputs` (lists of ids); returns (values, indices)."""
+
+    out = []
+    with torch.inference_mode():
+        for ids in inputs:
+            state = decoder(torch.tensor([ids], device=device))
+            out.append((state.topk_values.reshape(-1).clone(), state.topk_indices.reshape(-1).clone()))
+    decoder.check_errors()
+    return out
+
+
 def greedy(decoder, ids, steps):
     out = []
     with torch.inference_mode():
@@ -52,6 +68,49 @@ def greedy(decoder, ids, steps):
             ids = state.topk_indices[..., 0].reshape(1, 1)
     decoder.check_errors()
     return out
+
+
+def tolerance(value):
+    return 2e-2 + 2e-2 * abs(value)
+
+
+def check_teacher_forced(name, results, meta, failures):
+    """North-star top-k criteria per step, fed the golden run's inputs."""
+
+    for step, ((values, indices), record) in enumerate(zip(results, meta["steps"])):
+        ref_v = record["topk_values"]
+        values = values.cpu()
+        if not torch.allclose(values, torch.tensor(ref_v), rtol=2e-2, atol=2e-2):
+            failures.append("{} step {}: values {} vs golden {}".format(name, step, values.tolist(), ref_v))
+        for j in range(len(ref_v)):
+            tol = tolerance(ref_v[j])
+            before = ref_v[j - 1] - ref_v[j] if j else float("inf")
+            after = ref_v[j] - ref_v[j + 1] if j + 1 < len(ref_v) else record["k_k1_gap"]
+            if before > tol and after > tol and int(indices[j]) != record["topk_indices"][j]:
+                failures.append("{} step {}: id {} at rank {} vs golden {}".format(
+                    name, step, int(indices[j]), j, record["topk_indices"][j]))
+
+
+def check_greedy(name, results, meta, failures):
+    """Free-running greedy ids equal the golden ones up to the first step whose
+    golden top-1 / top-2 gap is inside the tolerance; there the engine must
+    pick one of the tied candidates, and the sequences may part."""
+
+    matched = 0
+    for step, ((values, indices), record) in enumerate(zip(results, meta["steps"])):
+        ref_v, ref_i = record["topk_values"], record["topk_indices"]
+        got = int(indices[0])
+        if got == meta["greedy_ids"][step]:
+            matched += 1
+            continue
+        tied = [ref_i[j] for j in range(len(ref_v)) if ref_v[0] - ref_v[j] <= tolerance(ref_v[0])]
+        if got not in tied or len(tied) < 2:
+            failures.append("{} step {}: greedy id {} vs golden {} (tied set {})".format(
+                name, step, got, meta["greedy_ids"][step], tied))
+        print("{}: greedy ids equal the golden run for {} steps, then a near-tie at step {} "
+              "(golden top-2 gap {:.4f})".format(name, matched, step, ref_v[0] - ref_v[1]))
+        return
+    print("{}: greedy ids equal the golden run for all {} steps".format(name, matched))
 
 
 def main():
@@ -65,31 +124,32 @@ def main():
     meta = json.load(open(os.path.join(HERE, "golden", "config0.json")))
     weights = TensorParallelWeights.seeded(world, rank, device, seed=meta["weight_seed"])
     ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(device)
+    inputs = [record["input_ids"] for record in meta["steps"]]
     runs = {}
     for exchange in ("peer", "nccl"):
         decoder = TensorParallelDecoder(Config(), weights, top_k=meta["top_k"], exchange=exchange)
-        runs[exchange] = greedy(decoder, ids, 1 + meta["decode_steps"])
+        runs[exchange, "forced"] = run(decoder, device, inputs)
+        decoder.close()
+        decoder = TensorParallelDecoder(Config(), weights, top_k=meta["top_k"], exchange=exchange)
+        runs[exchange, "greedy"] = greedy(decoder, ids, 1 + meta["decode_steps"])
         decoder.close()
     failures = []
-    for exchange, run in runs.items():
-        for step, (values, indices) in enumerate(run):
+    for key, results in runs.items():
+        for step, (values, indices) in enumerate(results):
             both = torch.cat([values.view(torch.int32).to(torch.int64), indices])
             gathered = torch.empty((world,) + tuple(both.shape), dtype=both.dtype, device=device)
             dist.all_gather_into_tensor(gathered, both)
             if not all(torch.equal(gathered[0], gathered[q]) for q in range(world)):
-                failures.append("{} step {}: ranks disagree".format(exchange, step))
+                failures.append("{} step {}: ranks disagree".format(key, step))
     if rank == 0:
-        for exchange, run in runs.items():
-            for step, ((values, indices), record) in enumerate(zip(run, meta["steps"])):
-                ref = torch.tensor(record["topk_values"])
-                if not torch.allclose(values.cpu(), ref, rtol=2e-2, atol=2e-2):
-                    failures.append("{} step {}: top-k values {} vs golden {}".format(
-                        exchange, step, values.cpu().tolist(), ref.tolist()))
-                if step < 8 and int(indices[0]) != meta["greedy_ids"][step]:
-                    failures.append("{} step {}: greedy id {} vs golden {}".format(
-                        exchange, step, int(indices[0]), meta["greedy_ids"][step]))
+        for exchange in ("peer", "nccl"):
+            check_teacher_forced(exchange, runs[exchange, "forced"], meta, failures)
+            check_greedy(exchange, runs[exchange, "greedy"], meta, failures)
+            worst = max(float((v.cpu() - torch.tensor(r["topk_values"])).abs().max())
+                        for (v, i), r in zip(runs[exchange, "forced"], meta["steps"]))
+            print("{}: largest top-k value difference from the golden run {:.4f}".format(exchange, worst))
         same_bits = all(torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
-                        for a, b in zip(runs["peer"], runs["nccl"]))
+                        for a, b in zip(runs["peer", "forced"], runs["nccl", "forced"]))
         print("world {}: peer and NCCL exchanges bit-identical: {}".format(world, same_bits))
         for line in failures:
             print("FAIL", line)
