@@ -381,6 +381,9 @@ struct GemvShape {
   // WARPS / WK warp rows work on different units at the same time
   static constexpr int WK = GROUPS % 8 == 0 ? 8 : GROUPS % 4 == 0 ? 4 : GROUPS % 2 == 0 ? 2 : 1;
   static constexpr int UL = WARPS / WK;          // units in flight side by side
+  // K-part and unit lane of warp w (compile-time 0 lane when UL == 1)
+  static __device__ __forceinline__ int kpart(unsigned w) { return UL == 1 ? int(w) : int(w % WK); }
+  static __device__ __forceinline__ int ulane(unsigned w) { return UL == 1 ? 0 : int(w / WK); }
   static constexpr int KS = K / WK;              // K-slice of each warp
   static constexpr int CPL = KS / 256;           // 16-byte chunks per lane per row slice
   static constexpr int UB = DEPTH * ((16 / (2 * CPL)) > 0 ? 16 / (2 * CPL) : 1);  // units per warp per batch
@@ -416,7 +419,7 @@ __device__ __forceinline__ void gemv_rows(const GemvParams& p, int u, const uint
   gemv_locate(p, u, seg, j);
   const Segment& sg = p.seg[seg];
   const int64_t row = int64_t(j / sg.group) * sg.group_stride + (j % sg.group);
-  const int kbase = ((threadIdx.x >> 5) % S::WK) * S::KS + (threadIdx.x & 31) * 8;
+  const int kbase = S::kpart(threadIdx.x >> 5) * S::KS + (threadIdx.x & 31) * 8;
   ra = sg.a_base + row * K + kbase;
   rb = sg.b_base + row * K + kbase;
 }
@@ -424,7 +427,7 @@ __device__ __forceinline__ void gemv_rows(const GemvParams& p, int u, const uint
 template <int K, int DEPTH = 1>
 __device__ __forceinline__ void gemv_load_batch(const GemvParams& p, int ub, int u1, GemvRegs<K, DEPTH>& r) {
   using S = GemvShape<K, DEPTH>;
-  const int ul = (threadIdx.x >> 5) / S::WK;
+  const int ul = S::ulane(threadIdx.x >> 5);
 #pragma unroll
   for (int i = 0; i < S::UB; ++i) {
     const int u = ub + i * S::UL + ul;
@@ -443,25 +446,6 @@ __device__ __forceinline__ void gemv_load_batch(const GemvParams& p, int ub, int
 __device__ __forceinline__ void gemv_cta_units(const GemvParams& p, int cta, int ncta, int& u0, int& u1) {
   u0 = int(int64_t(p.total_units) * cta / ncta);
   u1 = int(int64_t(p.total_units) * (cta + 1) / ncta);
-}
-
-// Ask L2 for the first rows of this CTA's unit range (up to `budget` bytes,
-// whole rows), one bulk prefetch per row, issued by different threads.
-// Weights never depend on the step, so this can run before a grid barrier:
-// HBM keeps streaming while the barrier completes.
-template <int K>
-__device__ __forceinline__ void gemv_prefetch_l2(const GemvParams& p, int cta, int ncta, int budget) {
-  int u0, u1;
-  gemv_cta_units(p, cta, ncta, u0, u1);
-  const int rows = min(2 * (u1 - u0), budget / (K * 2));
-  if (int(threadIdx.x) < rows) {
-    const int u = u0 + threadIdx.x / 2;
-    int seg, j;
-    gemv_locate(p, u, seg, j);
-    const Segment& sg = p.seg[seg];
-    const int64_t row = int64_t(j / sg.group) * sg.group_stride + (j % sg.group);
-    bulk_prefetch_l2((threadIdx.x & 1 ? sg.b_base : sg.a_base) + row * K, K * 2);
-  }
 }
 
 // Issue the first batch of this CTA's weight loads. Weights never depend on
@@ -491,7 +475,7 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   gemv_cta_units(p, cta, ncta, u0, u1);
   const int units = u1 - u0;
   float* lrow = part + size_t(units) * 2 * S::WK;  // EPI_TOPK: this CTA's logits
-  const int kp = warp % S::WK, ul = warp / S::WK;  // K-part and unit lane of this warp
+  const int kp = S::kpart(warp), ul = S::ulane(warp);  // K-part and unit lane of this warp
   const int kbase = kp * S::KS + lane * 8;
 
   float inv = 1.0f;
