@@ -42,6 +42,9 @@ LAYER_BYTES = 32 * 436_207_616
 HEAD_BYTES = 1_050_673_152
 NORM_BYTES = 532_480
 GATE_UP_BYTES = 234_881_024
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate+up launch, from an ncu
+# capture (--set full) of `bench.py --micro gate_up` (bytes per launch)
+GATE_UP_TRAFFIC = 239_350_000
 
 
 # algorithmic bytes per launch of the kernels timed by --micro
@@ -527,7 +530,8 @@ def tensor_parallel(args, world, rank, local, device):
         "roofline": {
             "bound": "hbm", "kernel": "gemv gate_up_swiglu shard (K=4096, N=2x{})".format(14336 // world),
             "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": None,
+            "frac": round(achieved / peak, 4), "traffic": GATE_UP_TRAFFIC // world,
+            "traffic_note": "single-GPU capture scaled by the rows a rank streams",
             "ms_per_launch": round(gate_up_ms, 5), "bytes_per_launch": gate_up_bytes,
         },
         "step_roofline": {
@@ -622,7 +626,7 @@ def main():
         "roofline": {
             "bound": "hbm", "kernel": "gemv gate_up_swiglu (K=4096, N=2x14336)",
             "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": None,
+            "frac": round(achieved / peak, 4), "traffic": GATE_UP_TRAFFIC,
             "ms_per_launch": round(gate_up_ms, 5), "bytes_per_launch": GATE_UP_BYTES,
         },
         "step_roofline": {
