@@ -176,6 +176,22 @@ __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// torch's silu on a bf16 tensor: x / (1 + exp(-x)) in fp32, rounded to bf16
+__device__ __forceinline__ float silu_bf16(float g) { return rbf(g / (1.0f + expf(-g))); }
+
+// RoPE of one (d, d+64) pair of a head at position `pos` (transformers
+// modeling_llama.py:124-168): the projection outputs a, b are rounded to bf16,
+// cos/sin of (inv_freq[d] * pos) in fp32 are cast to bf16, and
+// q*cos + rotate_half(q)*sin is evaluated with a bf16 rounding after each op.
+__device__ __forceinline__ void rope_pair(float a, float b, float inv_freq_d, int pos, uint16_t& out_a,
+                                          uint16_t& out_b) {
+  const float freq = inv_freq_d * float(pos);
+  const float c = rbf(cosf(freq)), s = rbf(sinf(freq));
+  const float qa = rbf(a), qb = rbf(b);
+  out_a = f2bf(rbf(qa * c) + rbf(-qb * s));
+  out_b = f2bf(rbf(qb * c) + rbf(qa * s));
+}
+
 // dot of 8 bf16 weights with 8 bf16 activations, accumulated in fp32
 __device__ __forceinline__ float dot8(const uint4 w, const uint4 x, float acc) {
   acc = fmaf(bf16lo(w.x), bf16lo(x.x), acc);

@@ -284,11 +284,6 @@ __device__ __forceinline__ uint4 ld_stream(const uint16_t* p) {
   return r;
 }
 
-__device__ __forceinline__ float silu_bf16(float g) {
-  // torch's silu on a bf16 tensor: x / (1 + exp(-x)) in fp32, rounded
-  return rbf(g / (1.0f + expf(-g)));
-}
-
 static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int j, float a, float b,
                               int pos) {
   int64_t oa = int64_t(j / sg.group) * sg.head_stride + (j % sg.group);
@@ -312,12 +307,10 @@ static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int
     case EPI_ROPE: {
       // transformers modeling_llama.py:124-168: cos/sin of (inv_freq * pos)
       // in fp32, cast to bf16; q*cos + rotate_half(q)*sin in bf16.
-      const int d = j % sg.group;
-      const float freq = __ldg(p.inv_freq + d) * float(pos);
-      const float c = rbf(cosf(freq)), s = rbf(sinf(freq));
-      const float qa = rbf(a), qb = rbf(b);
-      sg.out[oa] = f2bf(rbf(qa * c) + rbf(-qb * s));
-      sg.out[ob] = f2bf(rbf(qb * c) + rbf(qa * s));
+      uint16_t ra, rb;
+      rope_pair(a, b, __ldg(p.inv_freq + j % sg.group), pos, ra, rb);
+      sg.out[oa] = ra;
+      sg.out[ob] = rb;
       break;
     }
     case EPI_SILU:

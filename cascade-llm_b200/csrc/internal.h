@@ -38,6 +38,7 @@ int configure_smem(const char* what, void (*kernel)(KArgs...), size_t bytes) {
 
 int prepare_gemv();
 int prepare_attention();
+int prepare_gemm();
 
 // Launch `kernel<<<grid, block, smem, stream>>>(args...)` through
 // cudaLaunchKernelEx, adding the programmatic-stream-serialization attribute

@@ -220,6 +220,7 @@ extern "C" int cb_sm_count(void) { return sm_count(); }
 extern "C" int cb_prepare(void) {
   int rc = prepare_gemv();
   if (rc == kOk) rc = prepare_attention();
+  if (rc == kOk) rc = prepare_gemm();
   return rc;
 }
 extern "C" int cb_set_error_word(int32_t* device_word) {

@@ -51,6 +51,13 @@ _SIGNATURES = {
     "cb_lm_head_workspace_bytes": (_I64, [_I]),
     "cb_lm_head_topk": (_I, [_P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P, _P, _P, _P]),
     "cb_topk_merge": (_I, [_P, _P, _I, _P, _P, _I, _I, _P, _P, _P]),
+    "cb_gemm_bf16": (_I, [_P, _I, _I, _P, _I, _P, _P]),
+    "cb_gemm_residual": (_I, [_P, _I, _I, _P, _I, _P, _P, _P]),
+    "cb_gemm_partial": (_I, [_P, _I, _I, _P, _I, _P, _P]),
+    "cb_gemm_silu": (_I, [_P, _I, _P, _I, _P, _P]),
+    "cb_gemm_mul": (_I, [_P, _I, _P, _I, _P, _P]),
+    "cb_gemm_swiglu": (_I, [_P, _I, _P, _P, _I, _P, _P]),
+    "cb_prefill_qkv_rope": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _I64, _P]),
     "cb_exchange_bytes": (_I64, []),
     "cb_exchange_alloc": (_I, [_PP]),
     "cb_exchange_free": (_I, [_P]),

@@ -8,14 +8,21 @@ reference is replaced by one fused kernel per transfer unit:
 ==============  =====================================================  ============================
 unit            reference ops (llama31.py)                             kernel (torch.ops.cascade)
 ==============  =====================================================  ============================
-qkv / q,k,v     RMSNorm :173-179, 3x F.linear :241-245, RoPE :206-212,  qkv_rope
-                KV-cache cat :44-50
+qkv / q,k,v     RMSNorm :173-179, 3x F.linear :241-245, RoPE :206-212,  qkv_rope (prefill:
+                KV-cache cat :44-50                                    rmsnorm + prefill_qkv_rope)
 o_proj          repeat_kv + SDPA :182-234, F.linear + residual :246-250 attention, proj_residual
+                                                                       (prefill: gemm_residual)
 gate_up / g,u   RMSNorm :255-263, F.linear, silu :264-271              gate_up_swiglu (gate_silu,
-                                                                       up_mul for ``matrix``)
-down_proj       gate*up, F.linear + residual :272-280                 proj_residual
+                                                                       up_mul for ``matrix``;
+                                                                       prefill: gemm_swiglu)
+down_proj       gate*up, F.linear + residual :272-280                 proj_residual (prefill:
+                                                                       gemm_residual)
 finish          RMSNorm :325-329, LM head + topk :330-348              lm_head_topk (+ vocab path)
 ==============  =====================================================  ============================
+
+Multi-token steps (the prompt) run the fused units as tcgen05 tensor-core
+GEMMs over all the step's tokens; the ``matrix`` granularity's separate q/k/v
+and gate/up units keep the per-token GEMVs.
 
 The KV cache is pre-allocated (:class:`StaticKVCache`, ``[layers, 2, 8,
 capacity, 128]``) and the request position is a device counter, so a
@@ -248,6 +255,7 @@ class Llama31DecodeExecutor:
         rows = max(rows, 2 * self._rows)
         dev = self.device
         self._x = torch.empty((rows, 4096), dtype=torch.bfloat16, device=dev)
+        self._xn = torch.empty((rows, 4096), dtype=torch.bfloat16, device=dev)  # normalised rows (prefill)
         self._q = torch.empty((rows, 4096), dtype=torch.bfloat16, device=dev)
         self._attn = torch.empty((rows, 4096), dtype=torch.bfloat16, device=dev)
         self._mlp = torch.empty((rows, 14336), dtype=torch.bfloat16, device=dev)
@@ -314,7 +322,17 @@ class Llama31DecodeExecutor:
         norm_post = res["model.layers.{}.post_attention_layernorm.weight".format(layer)]
         w = lambda name: weights[_matrix_key(layer, name)]
         kc, vc = cache.key(layer), cache.value(layer)
-        if operation in ("qkv", "q_proj", "k_proj", "v_proj"):
+        # multi-token steps (prefill) run the fused units as tcgen05 GEMMs
+        gemm = tokens > 1
+        if operation in ("qkv", "q_proj", "k_proj", "v_proj") and gemm:
+            wq = w("q_proj") if operation in ("qkv", "q_proj") else None
+            wk = w("k_proj") if operation in ("qkv", "k_proj") else None
+            wv = w("v_proj") if operation in ("qkv", "v_proj") else None
+            ops.rmsnorm(self._x[:tokens], norm_in, eps, self._xn[:tokens])
+            ops.prefill_qkv_rope(self._xn[:tokens], wq, wk, wv, self.inv_freq, pos,
+                                 self._q[:tokens] if wq is not None else None,
+                                 kc if wk is not None else None, vc if wv is not None else None)
+        elif operation in ("qkv", "q_proj", "k_proj", "v_proj"):
             wq = w("q_proj") if operation in ("qkv", "q_proj") else None
             wk = w("k_proj") if operation in ("qkv", "k_proj") else None
             wv = w("v_proj") if operation in ("qkv", "v_proj") else None
@@ -330,12 +348,23 @@ class Llama31DecodeExecutor:
             ws = self._attention_workspace(tokens, splits)
             ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
             wo = w("o_proj")
-            for m in range(tokens):
-                ops.proj_residual(self._attn[m], wo, self._x[m], self._x[m])
+            if gemm:
+                ops.gemm_residual(self._attn[:tokens], wo, self._x[:tokens], self._x[:tokens])
+            else:
+                ops.proj_residual(self._attn[0], wo, self._x[0], self._x[0])
         elif operation == "gate_up":
             wg, wu = w("gate_proj"), w("up_proj")
-            for m in range(tokens):
-                ops.gate_up_swiglu(self._x[m], norm_post, eps, wg, wu, self._mlp[m])
+            if gemm:
+                ops.rmsnorm(self._x[:tokens], norm_post, eps, self._xn[:tokens])
+                ops.gemm_swiglu(self._xn[:tokens], wg, wu, self._mlp[:tokens])
+            else:
+                ops.gate_up_swiglu(self._x[0], norm_post, eps, wg, wu, self._mlp[0])
+        elif operation in ("gate_proj", "up_proj") and gemm:
+            ops.rmsnorm(self._x[:tokens], norm_post, eps, self._xn[:tokens])
+            if operation == "gate_proj":
+                ops.gemm_silu(self._xn[:tokens], w("gate_proj"), self._mlp[:tokens])
+            else:
+                ops.gemm_mul(self._xn[:tokens], w("up_proj"), self._mlp[:tokens])
         elif operation == "gate_proj":
             for m in range(tokens):
                 ops.gate_silu(self._x[m], norm_post, eps, w("gate_proj"), self._mlp[m])
@@ -344,8 +373,10 @@ class Llama31DecodeExecutor:
                 ops.up_mul(self._x[m], norm_post, eps, w("up_proj"), self._mlp[m])
         elif operation == "down_proj":
             wd = w("down_proj")
-            for m in range(tokens):
-                ops.proj_residual(self._mlp[m], wd, self._x[m], self._x[m])
+            if gemm:
+                ops.gemm_residual(self._mlp[:tokens], wd, self._x[:tokens], self._x[:tokens])
+            else:
+                ops.proj_residual(self._mlp[0], wd, self._x[0], self._x[0])
         else:
             raise ValueError("unknown Llama operation {}".format(operation))
 

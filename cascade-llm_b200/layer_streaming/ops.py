@@ -45,6 +45,16 @@ _SCHEMAS = {
         "Tensor(a!) out, Tensor(b!) workspace, Tensor(c!) tickets) -> ()"
     ),
     "position_set": "position_set(Tensor(a!) position, Tensor? src, int value) -> ()",
+    "gemm_bf16": "gemm_bf16(Tensor a, Tensor w, Tensor(a!) out) -> ()",
+    "gemm_residual": "gemm_residual(Tensor a, Tensor w, Tensor residual, Tensor(a!) out) -> ()",
+    "gemm_swiglu": "gemm_swiglu(Tensor a, Tensor w_gate, Tensor w_up, Tensor(a!) out) -> ()",
+    "gemm_partial": "gemm_partial(Tensor a, Tensor w, Tensor(a!) out) -> ()",
+    "gemm_silu": "gemm_silu(Tensor a, Tensor w_gate, Tensor(a!) out) -> ()",
+    "gemm_mul": "gemm_mul(Tensor a, Tensor w_up, Tensor(a!) gate_act) -> ()",
+    "prefill_qkv_rope": (
+        "prefill_qkv_rope(Tensor xn, Tensor? wq, Tensor? wk, Tensor? wv, Tensor inv_freq, Tensor position, "
+        "Tensor(a!)? q_out, Tensor(b!)? k_cache, Tensor(c!)? v_cache, int q_heads=32, int kv_heads=8) -> ()"
+    ),
     "position_advance": "position_advance(Tensor(a!) position, int count) -> ()",
 }
 
@@ -200,6 +210,84 @@ def attention(q, k_cache, v_cache, position, splits, chunk, out, workspace, tick
             nat.ptr(tickets, torch.int32, "tickets"), _stream(q),
         ),
         "cascade.attention",
+    )
+
+
+def _rows(t):
+    return t.numel() // t.shape[-1]
+
+
+def gemm_bf16(a, w, out):
+    nat.check(
+        nat.lib().cb_gemm_bf16(
+            nat.ptr(a, BF16, "a"), _rows(a), a.shape[-1], nat.ptr(w, BF16, "w"), w.shape[0],
+            nat.ptr(out, BF16, "out"), _stream(a),
+        ),
+        "cascade.gemm_bf16",
+    )
+
+
+def gemm_residual(a, w, residual, out):
+    nat.check(
+        nat.lib().cb_gemm_residual(
+            nat.ptr(a, BF16, "a"), _rows(a), a.shape[-1], nat.ptr(w, BF16, "w"), w.shape[0],
+            nat.ptr(residual, BF16, "residual"), nat.ptr(out, BF16, "out"), _stream(a),
+        ),
+        "cascade.gemm_residual",
+    )
+
+
+def gemm_partial(a, w, out):
+    nat.check(
+        nat.lib().cb_gemm_partial(
+            nat.ptr(a, BF16, "a"), _rows(a), a.shape[-1], nat.ptr(w, BF16, "w"), w.shape[0],
+            nat.ptr(out, torch.float32, "out"), _stream(a),
+        ),
+        "cascade.gemm_partial",
+    )
+
+
+def gemm_silu(a, w_gate, out):
+    nat.check(
+        nat.lib().cb_gemm_silu(
+            nat.ptr(a, BF16, "a"), _rows(a), nat.ptr(w_gate, BF16, "w_gate"), w_gate.shape[0],
+            nat.ptr(out, BF16, "out"), _stream(a),
+        ),
+        "cascade.gemm_silu",
+    )
+
+
+def gemm_mul(a, w_up, gate_act):
+    nat.check(
+        nat.lib().cb_gemm_mul(
+            nat.ptr(a, BF16, "a"), _rows(a), nat.ptr(w_up, BF16, "w_up"), w_up.shape[0],
+            nat.ptr(gate_act, BF16, "gate_act"), _stream(a),
+        ),
+        "cascade.gemm_mul",
+    )
+
+
+def gemm_swiglu(a, w_gate, w_up, out):
+    nat.check(
+        nat.lib().cb_gemm_swiglu(
+            nat.ptr(a, BF16, "a"), _rows(a), nat.ptr(w_gate, BF16, "w_gate"), nat.ptr(w_up, BF16, "w_up"),
+            w_gate.shape[0], nat.ptr(out, BF16, "out"), _stream(a),
+        ),
+        "cascade.gemm_swiglu",
+    )
+
+
+def prefill_qkv_rope(xn, wq, wk, wv, inv_freq, position, q_out, k_cache, v_cache, q_heads=32, kv_heads=8):
+    nat.check(
+        nat.lib().cb_prefill_qkv_rope(
+            nat.ptr(xn, BF16, "xn"), _rows(xn), nat.ptr(wq, BF16, "wq"), nat.ptr(wk, BF16, "wk"),
+            nat.ptr(wv, BF16, "wv"), int(q_heads), int(kv_heads), nat.ptr(inv_freq, torch.float32, "inv_freq"),
+            nat.ptr(position, torch.int32, "position"), nat.ptr(q_out, BF16, "q_out"),
+            nat.ptr(k_cache, BF16, "k_cache"), nat.ptr(v_cache, BF16, "v_cache"),
+            (k_cache if k_cache is not None else v_cache).shape[-2] if (k_cache is not None or v_cache is not None)
+            else 0, _stream(xn),
+        ),
+        "cascade.prefill_qkv_rope",
     )
 
 

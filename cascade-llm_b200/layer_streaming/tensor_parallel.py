@@ -337,6 +337,7 @@ class TensorParallelDecoder:
         dev = self.device
         local = self.q_heads * HEAD_DIM
         self._x = torch.empty((rows, HIDDEN), dtype=torch.bfloat16, device=dev)
+        self._xn = torch.empty((rows, HIDDEN), dtype=torch.bfloat16, device=dev)  # normalised rows (prefill)
         self._q = torch.empty((rows, local), dtype=torch.bfloat16, device=dev)
         self._attn = torch.empty((rows, local), dtype=torch.bfloat16, device=dev)
         self._mlp = torch.empty((rows, self.ffn), dtype=torch.bfloat16, device=dev)
@@ -390,8 +391,10 @@ class TensorParallelDecoder:
                 "cb_proj_allreduce_residual",
             )
             return
-        for m in range(tokens):
-            ops.proj_partial(source[m], weight, self._partial[m])
+        if tokens > 1:
+            ops.gemm_partial(source[:tokens], weight, self._partial[:tokens])
+        else:
+            ops.proj_partial(source[0], weight, self._partial[0])
         self.group.all_reduce(self._partial[:tokens])
         ops.residual_add_f32(self._x[:tokens], self._partial[:tokens], self._x[:tokens])
 
@@ -402,16 +405,25 @@ class TensorParallelDecoder:
         kc, vc = cache.key(layer), cache.value(layer)
         norm_in = w["model.layers.{}.input_layernorm.weight".format(layer)]
         norm_post = w["model.layers.{}.post_attention_layernorm.weight".format(layer)]
-        for m in range(tokens):
-            ops.qkv_rope(self._x[m], norm_in, self.eps, self._w(layer, "q_proj"), self._w(layer, "k_proj"),
-                         self._w(layer, "v_proj"), self.inv_freq, pos, m, self._q[m], kc, vc,
+        if tokens > 1:  # prefill: tcgen05 GEMM over the step's tokens
+            ops.rmsnorm(self._x[:tokens], norm_in, self.eps, self._xn[:tokens])
+            ops.prefill_qkv_rope(self._xn[:tokens], self._w(layer, "q_proj"), self._w(layer, "k_proj"),
+                                 self._w(layer, "v_proj"), self.inv_freq, pos, self._q[:tokens], kc, vc,
+                                 self.q_heads, self.kv_heads)
+        else:
+            ops.qkv_rope(self._x[0], norm_in, self.eps, self._w(layer, "q_proj"), self._w(layer, "k_proj"),
+                         self._w(layer, "v_proj"), self.inv_freq, pos, 0, self._q[0], kc, vc,
                          self.q_heads, self.kv_heads)
         ws = self._attention_workspace(tokens, splits)
         ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
         self._proj(layer, 0, self._attn, self._w(layer, "o_proj"), tokens, fused)
-        for m in range(tokens):
-            ops.gate_up_swiglu(self._x[m], norm_post, self.eps, self._w(layer, "gate_proj"),
-                               self._w(layer, "up_proj"), self._mlp[m])
+        if tokens > 1:
+            ops.rmsnorm(self._x[:tokens], norm_post, self.eps, self._xn[:tokens])
+            ops.gemm_swiglu(self._xn[:tokens], self._w(layer, "gate_proj"), self._w(layer, "up_proj"),
+                            self._mlp[:tokens])
+        else:
+            ops.gate_up_swiglu(self._x[0], norm_post, self.eps, self._w(layer, "gate_proj"),
+                               self._w(layer, "up_proj"), self._mlp[0])
         self._proj(layer, 1, self._mlp, self._w(layer, "down_proj"), tokens, fused)
 
     def _head(self, tokens):

@@ -177,6 +177,38 @@ int cb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache
                          const int32_t* position, int M, int splits, int chunk, void* out,
                          void* stream);
 
+/* ------------------------------------------------------------- prefill */
+
+/* Prefill projections of an M-token chunk on the tcgen05 tensor cores
+ * (BF16 in, FP32 accumulate in TMEM, bf16 out): the F.linear calls of
+ * llama31.py:238-280 with M > 1. A / xn: [M, K] row-major activations; W:
+ * [N, K] row-major weights; K a multiple of 64; all pointers 16-byte
+ * aligned. Rounding points are those of the decode kernels.
+ *   cb_gemm_bf16:        out[M, N] = bf16(A . W^T); N a multiple of 128
+ *   cb_gemm_residual:    out = bf16(residual + bf16(A . W^T)) (out may be residual)
+ *   cb_gemm_partial:     out[M, N] = A . W^T in fp32 (a tensor-parallel partial sum)
+ *   cb_gemm_silu / cb_gemm_mul: the two halves of cb_gemm_swiglu for the `matrix`
+ *                        granularity (gate and up in separate units): out =
+ *                        bf16(silu(bf16(A . Wg^T))), then gate_act = bf16(gate_act *
+ *                        bf16(A . Wu^T)) in place
+ *   cb_gemm_swiglu:      out[M, rows] = bf16(silu(bf16(A . Wg^T)) * bf16(A . Wu^T)),
+ *                        K = 4096, rows a multiple of 128 (14336 or a rank's share)
+ *   cb_prefill_qkv_rope: q_out[M, 128*q_heads] = RoPE(xn . Wq^T); K/V of the M
+ *                        positions *position .. *position+M-1 written into the
+ *                        caches [kv_heads, cache_len, 128] (K after RoPE); any of
+ *                        wq / wk / wv may be NULL (the `matrix` granularity) */
+int cb_gemm_bf16(const void* a, int M, int K, const void* w, int N, void* out, void* stream);
+int cb_gemm_residual(const void* a, int M, int K, const void* w, int N, const void* residual, void* out,
+                     void* stream);
+int cb_gemm_partial(const void* a, int M, int K, const void* w, int N, float* out, void* stream);
+int cb_gemm_silu(const void* a, int M, const void* w_gate, int rows, void* out, void* stream);
+int cb_gemm_mul(const void* a, int M, const void* w_up, int rows, void* gate_act, void* stream);
+int cb_gemm_swiglu(const void* a, int M, const void* w_gate, const void* w_up, int rows, void* out,
+                   void* stream);
+int cb_prefill_qkv_rope(const void* xn, int M, const void* wq, const void* wk, const void* wv, int q_heads,
+                        int kv_heads, const float* inv_freq, const int32_t* position, void* q_out,
+                        void* k_cache, void* v_cache, int64_t cache_len, void* stream);
+
 /* ------------------------------------------------------ tensor parallelism */
 
 /* Decode across N GPUs of one node (one process per GPU), an addition to the

@@ -1,0 +1,159 @@
+"""Prefill GEMMs on the tcgen05 tensor cores against torch and the decode path.
+
+The GEMM accumulates in fp32 in a different order than cuBLAS, so a bf16
+output may sit one ulp away; each case is held to rtol/atol 1e-2 of the torch
+op with the mismatch fraction bounded, and to be at least as close to the
+fp64 result as torch's own bf16 output (plus one bf16 ulp of slack). The fused
+epilogues (residual, SwiGLU, RoPE + KV-cache write) are checked against the
+decode GEMV kernels, which share their rounding points.
+"""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import llama_oracle as lo
+
+pytestmark = pytest.mark.gpu
+
+BF16 = torch.bfloat16
+
+
+@pytest.fixture(scope="module")
+def ops(cuda):
+    from layer_streaming import _native
+    from layer_streaming import ops as cascade_ops
+
+    _native.check(_native.lib().cb_prepare(), "cb_prepare")
+    return cascade_ops
+
+
+def randn(shape, seed, std=1.0, device="cuda:0"):
+    gen = torch.Generator(device=device).manual_seed(seed)
+    return (torch.randn(shape, generator=gen, device=device) * std).to(BF16)
+
+
+def close_to_torch(got, a, w, extra=None):
+    ref = F.linear(a, w)
+    exact = a.double() @ w.double().T
+    if extra is not None:
+        ref = (extra.float() + ref.float()).to(BF16)
+        exact = extra.double() + exact
+    torch.testing.assert_close(got.float(), ref.float(), rtol=1e-2, atol=1e-2)
+    assert (got.float() != ref.float()).float().mean().item() <= 0.05
+    ulp = exact.abs().max().item() * 2.0 ** -8
+    assert (got.double() - exact).abs().max().item() <= (ref.double() - exact).abs().max().item() + ulp
+
+
+@pytest.mark.parametrize("m,k,n", [(128, 4096, 4096), (6, 4096, 6144), (200, 4096, 256), (512, 14336, 4096),
+                                   (64, 512, 4096), (300, 1792, 128)])
+def test_gemm_bf16_matches_torch(ops, cuda, m, k, n):
+    a = randn((m, k), 1000 + m, 1.0)
+    w = randn((n, k), 1001 + n, 0.02)
+    out = torch.full((m, n), 7.0, dtype=BF16, device=cuda)
+    ops.gemm_bf16(a, w, out)
+    torch.cuda.synchronize()
+    close_to_torch(out, a, w)
+
+
+@pytest.mark.parametrize("m,k", [(64, 4096), (512, 14336), (77, 2048)])
+def test_gemm_residual_matches_torch(ops, cuda, m, k):
+    a = randn((m, k), 1100 + m, 1.0)
+    w = randn((4096, k), 1101, 0.02)
+    res = randn((m, 4096), 1102, 1.0)
+    out = torch.empty_like(res)
+    ops.gemm_residual(a, w, res, out)
+    close_to_torch(out, a, w, extra=res)
+    # in place, as the prefill path uses it
+    res2 = res.clone()
+    ops.gemm_residual(a, w, res2, res2)
+    assert torch.equal(res2, out)
+
+
+@pytest.mark.parametrize("m,k", [(64, 512), (300, 14336)])
+def test_gemm_partial_is_the_unrounded_sum(ops, cuda, m, k):
+    a = randn((m, k), 1150 + m, 1.0)
+    w = randn((4096, k), 1151, 0.02)
+    part = torch.empty((m, 4096), dtype=torch.float32, device=cuda)
+    ops.gemm_partial(a, w, part)
+    exact = a.double() @ w.double().T
+    bound = 1e-6 * k ** 0.5 * (a.double().abs() @ w.double().abs().T) + 1e-6
+    assert bool(((part.double() - exact).abs() <= 8 * bound).all())
+    # rounded, it is the plain GEMM's output
+    out = torch.empty((m, 4096), dtype=BF16, device=cuda)
+    ops.gemm_bf16(a, w, out)
+    assert torch.equal(part.to(BF16), out)
+
+
+@pytest.mark.parametrize("m,rows", [(128, 14336), (33, 1792)])
+def test_gemm_swiglu_matches_decode_kernel(ops, cuda, m, rows):
+    a = randn((m, 4096), 1200 + m, 1.0)
+    wg, wu = randn((rows, 4096), 1201, 0.02), randn((rows, 4096), 1202, 0.02)
+    out = torch.empty((m, rows), dtype=BF16, device=cuda)
+    ops.gemm_swiglu(a, wg, wu, out)
+    ref = (F.silu(F.linear(a, wg)) * F.linear(a, wu)).float()
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    # the decode kernel on each row (no norm): same rounding points; silu(bf16(g)) * bf16(u)
+    # compounds a one-ulp difference of either factor, so two ulps (2e-2) apart at most
+    per_row = torch.empty_like(out)
+    for i in range(m):
+        ops.gate_up_swiglu(a[i], None, 1e-5, wg, wu, per_row[i])
+    torch.testing.assert_close(out.float(), per_row.float(), rtol=2e-2, atol=2e-2)
+    assert (out != per_row).float().mean().item() <= 0.05
+
+
+def test_split_swiglu_and_single_matrix_qkv_equal_the_fused_gemms(ops, cuda):
+    """The `matrix` granularity's separate units give the fused kernels' bits."""
+
+    m = 70
+    a = randn((m, 4096), 1250, 1.0)
+    wg, wu = randn((14336, 4096), 1251, 0.02), randn((14336, 4096), 1252, 0.02)
+    fused = torch.empty((m, 14336), dtype=BF16, device=cuda)
+    ops.gemm_swiglu(a, wg, wu, fused)
+    split = torch.empty_like(fused)
+    ops.gemm_silu(a, wg, split)
+    ops.gemm_mul(a, wu, split)
+    assert torch.equal(split, fused)
+    wq, wk, wv = randn((4096, 4096), 1253, 0.02), randn((1024, 4096), 1254, 0.02), randn((1024, 4096), 1255, 0.02)
+    inv = lo.llama3_inv_freq(device=cuda)
+    pos = torch.tensor([11], dtype=torch.int32, device=cuda)
+    q = torch.empty((m, 4096), dtype=BF16, device=cuda)
+    kc = torch.zeros((8, 100, 128), dtype=BF16, device=cuda)
+    vc = torch.zeros_like(kc)
+    ops.prefill_qkv_rope(a, wq, wk, wv, inv, pos, q, kc, vc)
+    q2, kc2, vc2 = torch.empty_like(q), torch.zeros_like(kc), torch.zeros_like(vc)
+    ops.prefill_qkv_rope(a, wq, None, None, inv, pos, q2, None, None)
+    ops.prefill_qkv_rope(a, None, wk, None, inv, pos, None, kc2, None)
+    ops.prefill_qkv_rope(a, None, None, wv, inv, pos, None, None, vc2)
+    assert torch.equal(q2, q) and torch.equal(kc2, kc) and torch.equal(vc2, vc)
+
+
+@pytest.mark.parametrize("start,m,q_heads,kv_heads", [(0, 6, 32, 8), (100, 128, 32, 8), (7, 200, 8, 2)])
+def test_prefill_qkv_rope_matches_decode_kernel(ops, cuda, start, m, q_heads, kv_heads):
+    xn = randn((m, 4096), 1300 + m, 1.0)
+    wq = randn((q_heads * 128, 4096), 1301, 0.02)
+    wk = randn((kv_heads * 128, 4096), 1302, 0.02)
+    wv = randn((kv_heads * 128, 4096), 1303, 0.02)
+    inv = lo.llama3_inv_freq(device=cuda)
+    cap = start + m + 5
+    pos = torch.tensor([start], dtype=torch.int32, device=cuda)
+    q = torch.empty((m, q_heads * 128), dtype=BF16, device=cuda)
+    kc = torch.full((kv_heads, cap, 128), 7.0, dtype=BF16, device=cuda)
+    vc = torch.full_like(kc, 7.0)
+    ops.prefill_qkv_rope(xn, wq, wk, wv, inv, pos, q, kc, vc, q_heads, kv_heads)
+    # the decode kernel, token by token (no norm: xn is already normalised)
+    q2 = torch.empty_like(q)
+    kc2 = torch.full_like(kc, 7.0)
+    vc2 = torch.full_like(kc, 7.0)
+    for i in range(m):
+        ops.qkv_rope(xn[i], None, 1e-5, wq, wk, wv, inv, pos, i, q2[i], kc2, vc2, q_heads, kv_heads)
+    torch.cuda.synchronize()
+    # RoPE subtracts two rounded products: a one-ulp difference of the projection
+    # (|q| ~ 2-4, ulp 1/64) can survive the cancellation, so the absolute bound is
+    # the projection's ulp rather than the output's
+    for got, ref in ((q, q2), (kc, kc2), (vc, vc2)):
+        torch.testing.assert_close(got.float(), ref.float(), rtol=1e-2, atol=2e-2)
+        assert (got != ref).float().mean().item() <= 0.05
+    # nothing outside the step's positions was written
+    outside = torch.cat([kc[:, :start], kc[:, start + m:], vc[:, :start], vc[:, start + m:]], dim=1)
+    assert bool((outside == 7.0).all())

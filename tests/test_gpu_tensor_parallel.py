@@ -24,6 +24,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
+import parity
 from conftest import REPO, golden_path
 from oracle.seeded import prompt_ids
 
@@ -220,10 +221,14 @@ def test_world_of_one_decoder_reproduces_golden_run(cuda):
         decoder.close()
     for (v1, i1), (v2, i2) in zip(runs["peer"], runs["nccl"]):
         assert torch.equal(v1, v2) and torch.equal(i1, i2)
+    gpu_topk = parity.reference_gpu_topk(weights.tensors, meta, cuda)
     for step, ((values, indices), record) in enumerate(zip(runs["peer"], meta["steps"])):
-        torch.testing.assert_close(values, torch.tensor(record["topk_values"]), rtol=2e-2, atol=2e-2)
-        if step < 8:
-            assert int(indices[0]) == meta["greedy_ids"][step]
+        failure = parity.topk_values_failure(values, record, gpu_topk[step])
+        assert failure is None, "step {}: {}".format(step, failure)
+        failure, tie = parity.greedy_failure(step, int(indices[0]), record, meta)
+        assert failure is None, "step {}: {}".format(step, failure)
+        if tie:
+            break  # free-running greedy decoding parts from the reference's after a near-tie
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
