@@ -58,6 +58,16 @@ MICRO_BYTES = {
 }
 
 
+# prefill GEMMs timed by --micro: (out features, in features) of one layer's
+# projection at M = --tokens rows
+GEMM_SHAPES = {
+    "gemm_qkv": (6144, 4096),
+    "gemm_o_proj": (4096, 4096),
+    "gemm_gate_up": (28672, 4096),
+    "gemm_down_proj": (4096, 14336),
+}
+
+
 def step_bytes(context):
     """Algorithmic HBM bytes of one decode token at `context` cached positions."""
 
@@ -72,11 +82,12 @@ def parse_args():
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--context", type=int, default=2048)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--tokens", type=int, default=512, help="rows of the --micro gemm_* cases")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--profile-range", action="store_true",
                         help="after warm-up, run --steps decode steps between cudaProfilerStart/Stop "
                              "(for `ncu --profile-from-start off`) and exit")
-    parser.add_argument("--micro", choices=sorted(MICRO_BYTES),
+    parser.add_argument("--micro", choices=sorted(MICRO_BYTES) + sorted(GEMM_SHAPES),
                         help="time one kernel alone on a small footprint (rotating copies > L2)")
     parser.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
                         help="N>1: tensor-parallel exchange through peer memory inside the projection "
@@ -101,13 +112,17 @@ class Config:
     }
 
 
-def measured_peak():
+def measured_peak(key="hbm_gbs"):
+    """(peak, "measured"|"fallback"): HBM GB/s, or dense bf16 TFLOP/s for
+    key="bf16_tflops" (burst) / "bf16_tflops_sustained"."""
+
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    fallback = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}[key]
     try:
         with open(path) as source:
-            return float(json.load(source)["hbm_gbs"]), "measured"
+            return float(json.load(source)[key]), "measured"
     except (OSError, KeyError, ValueError):
-        return 6650.0, "fallback"
+        return fallback, "fallback"
 
 
 class ClockSampler:
@@ -190,14 +205,20 @@ def step(executor, runtime, ids):
 
 
 def prefill(executor, runtime, device, context, chunk=512):
+    """Chunked prefill of `context` random ids; returns (next token, ms)."""
+
     ids = random_ids(context, seed=1).to(device)
     state = None
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.inference_mode():
-        for start in range(0, context, chunk):
-            state = step(executor, runtime, ids[:, start:start + chunk])
+        start.record()
+        for begin in range(0, context, chunk):
+            state = step(executor, runtime, ids[:, begin:begin + chunk])
+        end.record()
     torch.cuda.synchronize(device)
     executor.check_errors()
-    return state.topk_indices[..., 0]
+    return state.topk_indices[..., 0], start.elapsed_time(end)
 
 
 def time_decode(executor, runtime, token, steps, warmup, barrier):
@@ -300,6 +321,59 @@ def cpu_baseline(store, executor, context, budget_s):
     }
 
 
+def micro_gemm(args, device):
+    """One prefill projection GEMM of a layer (tcgen05), back to back over the
+    weights of 8 layers (> L2), at M = --tokens rows: TFLOP/s vs the measured
+    dense bf16 peak."""
+
+    from layer_streaming import _native, ops
+
+    _native.check(_native.lib().cb_prepare(), "cb_prepare")
+    bf = torch.bfloat16
+    name = args.micro
+    n, k = GEMM_SHAPES[name]
+    m = args.tokens
+    gen = torch.Generator(device=device).manual_seed(5)
+    a = (torch.randn((m, k), generator=gen, device=device)).to(bf)
+    layers = 8
+    if name == "gemm_gate_up":
+        mats = [((torch.randn((n // 2, k), generator=gen, device=device) * 0.02).to(bf),
+                 (torch.randn((n // 2, k), generator=gen, device=device) * 0.02).to(bf)) for _ in range(layers)]
+        out = torch.empty((m, n // 2), dtype=bf, device=device)
+        run = lambda w: ops.gemm_swiglu(a, w[0], w[1], out)
+    elif name == "gemm_qkv":
+        mats = [tuple((torch.randn((r, k), generator=gen, device=device) * 0.02).to(bf) for r in (4096, 1024, 1024))
+                for _ in range(layers)]
+        inv = torch.ones(64, device=device)
+        pos = torch.zeros(1, dtype=torch.int32, device=device)
+        q = torch.empty((m, 4096), dtype=bf, device=device)
+        kc = torch.empty((8, m, 128), dtype=bf, device=device)
+        vc = torch.empty_like(kc)
+        run = lambda w: ops.prefill_qkv_rope(a, w[0], w[1], w[2], inv, pos, q, kc, vc)
+    else:
+        mats = [(torch.randn((n, k), generator=gen, device=device) * 0.02).to(bf) for _ in range(layers)]
+        res = torch.randn((m, n), generator=gen, device=device).to(bf)
+        run = lambda w: ops.gemm_residual(a, w, res, res)
+    for i in range(args.warmup * layers):
+        run(mats[i % layers])
+    torch.cuda.synchronize()
+    launches = args.steps * layers
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(launches):
+        run(mats[i % layers])
+    end.record()
+    torch.cuda.synchronize()
+    us = start.elapsed_time(end) * 1000.0 / launches
+    flops = 2.0 * m * n * k
+    tflops = flops / (us * 1e-6) / 1e12
+    peak, kind = measured_peak("bf16_tflops")
+    print(json.dumps({"micro": name, "tokens": m, "us_per_launch": round(us, 3), "flop_per_launch": flops,
+                      "achieved_tflops": round(tflops, 1), "peak_tflops": peak, "peak_kind": kind,
+                      "frac": round(tflops / peak, 4), "weight_gbs": round(n * k * 2 / (us * 1e-6) / 1e9, 1),
+                      "launches": launches}), flush=True)
+
+
 def micro(args, device):
     """One kernel, back to back over rotating weight copies (> L2 in total)."""
 
@@ -309,6 +383,8 @@ def micro(args, device):
     _native.check(_native.lib().cb_prepare(), "cb_prepare")
     bf = torch.bfloat16
     name = args.micro
+    if name in GEMM_SHAPES:
+        return micro_gemm(args, device)
     copies = {"lm_head": 2, "gate_up": 2}.get(name, 6)
 
     def rnd(*shape, std=0.02):
@@ -434,11 +510,18 @@ def tensor_parallel(args, world, rank, local, device):
     decoder = TensorParallelDecoder(Config(), weights, top_k=10, max_length=args.context + extra,
                                     exchange=args.exchange)
     ids = random_ids(args.context, seed=1).to(device)
+    torch.cuda.synchronize(device)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.inference_mode():
+        p0.record()
         for start in range(0, args.context, 512):
             state = decoder(ids[:, start:start + 512])
+        p1.record()
     torch.cuda.synchronize(device)
     decoder.check_errors()
+    t = torch.tensor([p0.elapsed_time(p1)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    prefill_ms = float(t.item())
     token = state.topk_indices[..., 0].reshape(1, 1)
 
     def barrier():
@@ -539,6 +622,8 @@ def tensor_parallel(args, world, rank, local, device):
             "frac": round(rank_gbs / peak, 4), "bytes_per_token_per_rank": rank_bytes,
         },
         "cpu_baseline": None,
+        "prefill": {"tokens": args.context, "chunk": 512, "ms": round(prefill_ms, 2),
+                    "tokens_per_s": round(args.context / (prefill_ms / 1000.0), 1)},
         "gpu_launches": (1 + 32 * 5 + 1 + 2) * args.steps if args.exchange == "peer" else None,
         "clocks": clock_info,
     }
@@ -573,7 +658,7 @@ def main():
 
     extra = args.warmup + args.steps * 2 + 64
     plan, store, resident, runtime, executor = build_engine(device, args.context, extra)
-    token = prefill(executor, runtime, device, args.context)
+    token, prefill_ms = prefill(executor, runtime, device, args.context)
     if args.profile_range:
         with torch.inference_mode():
             for _ in range(args.warmup):
@@ -634,6 +719,11 @@ def main():
             "frac_of_8tbs": round(step_gbs / 8000.0, 4), "bytes_per_token": step_bytes(context),
         },
         "cpu_baseline": baseline,
+        "prefill": {
+            "tokens": args.context, "chunk": 512, "ms": round(prefill_ms, 2),
+            "tokens_per_s": round(args.context / (prefill_ms / 1000.0), 1),
+            "note": "first (cold) prefill through the API: tcgen05 GEMMs + split-KV attention per chunk",
+        },
         "gpu_launches": kernels_per_step * args.steps,
         "clocks": clock_info,
     }

@@ -15,6 +15,8 @@
 //   warp 2        allocates / frees the BN TMEM columns of the accumulator
 //   warps 4..7    epilogue: tcgen05.ld of their 32 TMEM lanes (= tile rows),
 //                 the mode's fused epilogue, bf16 stores
+// Grid: (M tiles, N tiles), M fastest, so the M tiles of one weight tile are
+// resident at the same time and the weights cross HBM about once.
 // Epilogues mirror the decode GEMV's rounding points: plain bf16 store,
 // residual add, SwiGLU (gate and up rows of the same FFN index in one tile),
 // and QKV with RoPE and the K/V cache write.
@@ -87,7 +89,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* acc_bar = empty + kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::TMEM_SLOT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kBM;
+  const int m0 = blockIdx.x * kBM;
   const int nk = p.K / kBK;
 
   if (threadIdx.x == 0) {
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const CUtensorMap* mb = &tb0;
       int yb = 0;
       if (MODE == GEMM_QKV_ROPE) {
-        const int n0 = blockIdx.x * BN;
+        const int n0 = blockIdx.y * BN;
         if (n0 < p.q_rows) {
           yb = n0;
         } else if (n0 < p.q_rows + p.k_rows) {
@@ -123,9 +125,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           yb = n0 - p.q_rows - p.k_rows;
         }
       } else if (MODE == GEMM_SWIGLU) {
-        yb = blockIdx.x * (BN / 2);
+        yb = blockIdx.y * (BN / 2);
       } else {
-        yb = blockIdx.x * BN;
+        yb = blockIdx.y * BN;
       }
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % kStages;
@@ -174,7 +176,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t taddr = tmem + (uint32_t((warp & 3) * 32) << 16);
     float v[32];
     if (MODE == GEMM_PARTIAL) {
-      const int n0 = blockIdx.x * BN;
+      const int n0 = blockIdx.y * BN;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         tmem_ld32(taddr + c * 32, v);
@@ -184,7 +186,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int q = 0; q < 8; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
       }
     } else if (MODE == GEMM_STORE || MODE == GEMM_RESIDUAL || MODE == GEMM_SILU || MODE == GEMM_MUL) {
-      const int n0 = blockIdx.x * BN;
+      const int n0 = blockIdx.y * BN;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         tmem_ld32(taddr + c * 32, v);
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     } else if (MODE == GEMM_SWIGLU) {
-      const int n0 = blockIdx.x * (BN / 2);
+      const int n0 = blockIdx.y * (BN / 2);
       float u[32];
 #pragma unroll 1
       for (int c = 0; c < BN / 64; ++c) {
@@ -239,7 +241,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     } else {  // GEMM_QKV_ROPE, BN == 128: one head per tile
-      const int n0 = blockIdx.x * BN;
+      const int n0 = blockIdx.y * BN;
       const int pos = __ldcg(p.pos) + m;
       const bool in_cache = pos >= 0 && pos < p.cache_len;
       if (live && n0 >= p.q_rows && !in_cache && p.err) atomicExch(p.err, 103);
@@ -345,7 +347,9 @@ int run_gemm(const char* what, const CUtensorMap& ta, const CUtensorMap& tb0, co
   int rc = configure_smem(what, gemm_kernel<BN, MODE>, GemmSmem<BN>::BYTES);
   if (rc != kOk) return rc;
   p.err = error_word();
-  const dim3 grid(grid_x, (p.M + kBM - 1) / kBM);
+  // M tiles vary fastest: the CTAs that share a weight tile run together and
+  // read it from DRAM once (L2 serves the others)
+  const dim3 grid((p.M + kBM - 1) / kBM, grid_x);
   return launch(what, gemm_kernel<BN, MODE>, grid, dim3(kGemmThreads), GemmSmem<BN>::BYTES, stream, ta, tb0, tb1,
                 tb2, p);
 }
@@ -383,7 +387,9 @@ static int gemm_linear(const char* what, int mode, const void* a, int M, int K, 
   if (mode == GEMM_RESIDUAL && (!residual || !aligned16(residual)))
     return fail(kErrInvalid, "%s: residual must be a 16-byte aligned device pointer", what);
   if (N < 128 || N % 128) return fail(kErrInvalid, "%s: N=%d must be a positive multiple of 128", what, N);
-  const int bn = N % 256 == 0 ? 256 : 128;
+  // 256-column tiles, unless they would leave SMs idle (one CTA per SM)
+  const int mtiles = (M + kBM - 1) / kBM;
+  const int bn = (N % 256 == 0 && int64_t(N / 256) * mtiles >= sm_count()) ? 256 : 128;
   CUtensorMap ta, tb;
   int rc = make_tile_map(&ta, what, a, M, K, kBM);
   if (rc == kOk) rc = make_tile_map(&tb, what, w, N, K, bn);
