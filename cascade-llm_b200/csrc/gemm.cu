@@ -8,7 +8,7 @@
 // One CTA computes a 128 x BN tile of C:
 //   warp 0        TMA producer: A (activations) and W (weights) K-blocks of 64
 //                 bf16, 128-byte swizzle, into a 4-stage shared-memory ring
-//                 (mbarriers full/empty per stage; no multicast)
+//                 (mbarriers full/empty per stage; each CTA loads its own tiles)
 //   warp 1        MMA issuer: one thread issues tcgen05.mma kind::f16
 //                 (M=128, N=BN, K=16; BF16 in, FP32 accumulate in TMEM) and
 //                 commits each stage back to the producer

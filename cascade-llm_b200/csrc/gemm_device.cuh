@@ -92,7 +92,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // ------------------------------------------------------------------ TMA
 // 2-D tiled bulk tensor load global -> shared (this CTA), completing its
 // bytes on `bar`. x is the innermost (K) coordinate in elements; it is always
-// a multiple of 64 bf16 here (128 bytes). No multicast.
+// a multiple of 64 bf16 here (128 bytes). The tile goes to this CTA only.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
