@@ -9,11 +9,14 @@ reference's tests use to run without a GPU.
 
 Additions: :meth:`BaseWeightStore.fill_seeded` writes the seeded random-init
 weights of the benchmark configurations (generated on the GPU by
-``cb_fill_normal_bf16``, norms = 1) and :meth:`load_checkpoint` reads each
-safetensors file once.
+``cb_fill_normal_bf16``, norms = 1); :meth:`load_checkpoint` parses each
+safetensors header once and reads the tensor bytes straight into the arena
+with parallel ``pread`` on native threads; the staging store's pageable ->
+pinned copies run on native threads (``cb_host_copy``).
 """
 
 import json
+import os
 import threading
 import time
 from concurrent.futures import Future, ThreadPoolExecutor
@@ -45,6 +48,22 @@ def _checkpoint_files(checkpoint):
     raise FileNotFoundError(
         "expected model.safetensors or model.safetensors.index.json in {}".format(checkpoint)
     )
+
+
+def _native_copy_ok(target, source):
+    """Both CPU, contiguous, same dtype and size, and the native library present."""
+
+    if target.device.type != "cpu" or source.device.type != "cpu" or target.dtype != source.dtype:
+        return False
+    if not (target.is_contiguous() and source.is_contiguous()) or target.numel() != source.numel():
+        return False
+    from . import _native
+
+    try:
+        _native.lib()
+    except (OSError, RuntimeError):
+        return False
+    return True
 
 
 def is_norm(key):
@@ -112,41 +131,32 @@ class BaseWeightStore:
     def required_keys(self):
         return sorted(k for k, s in self.plan.tensors.items() if s.alias_of is None)
 
-    def load_checkpoint(self, checkpoint):
-        """Copy a local safetensors checkpoint into the packed arena (as bf16)."""
+    def load_checkpoint(self, checkpoint, threads=0):
+        """Copy a local safetensors checkpoint into the packed arena (as bf16).
+
+        Each file's header is parsed once and every tensor's bytes are read
+        straight into its arena view by parallel ``pread`` on native threads
+        (``threads`` = 0: up to 16); non-BF16 tensors are converted.
+        """
+
+        from .checkpoint import load_safetensors_into
 
         if self.arena is None:
             self.allocate()
-        try:
-            from safetensors import safe_open
-        except ImportError as error:
-            raise RuntimeError("safetensors is required to load a checkpoint") from error
         required = set(self.required_keys())
         weight_map = _checkpoint_files(checkpoint)
         if weight_map is None:
-            files = [Path(checkpoint) / "model.safetensors"]
+            files = {key: Path(checkpoint) / "model.safetensors" for key in required}
         else:
             missing = required.difference(weight_map)
             if missing:
                 raise KeyError(
                     "checkpoint index misses required tensors: {}".format(", ".join(sorted(missing)[:8]))
                 )
-            files = sorted({weight_map[key] for key in required})
-        loaded = set()
+            files = {key: weight_map[key] for key in required}
+        targets = {key: self._view(key) for key in required}
         with torch.inference_mode():
-            for path in files:
-                with safe_open(str(path), framework="pt", device="cpu") as source:
-                    for key in sorted(required.intersection(source.keys())):
-                        tensor = source.get_tensor(key)
-                        target = self._view(key)
-                        if tuple(tensor.shape) != tuple(target.shape):
-                            raise ValueError(
-                                "{} shape {} != expected {}".format(
-                                    key, tuple(tensor.shape), tuple(target.shape)
-                                )
-                            )
-                        target.copy_(tensor.to(dtype=torch.bfloat16))
-                        loaded.add(key)
+            loaded = load_safetensors_into(files, targets, threads)
         missing = required.difference(loaded)
         if missing:
             raise KeyError("checkpoint misses required tensors: {}".format(", ".join(sorted(missing)[:8])))
@@ -218,9 +228,11 @@ class FullPinnedWeightStore(BaseWeightStore):
 class PinnedStagingWeightStore(BaseWeightStore):
     """Pageable full store plus reusable page-locked staging slots."""
 
-    def __init__(self, plan, allocate=True, tensor_factory=None, worker_count=2):
+    def __init__(self, plan, allocate=True, tensor_factory=None, worker_count=2, copy_threads=None):
         self.staging_slots = None
         self.worker_count = int(worker_count)
+        # native threads per staging copy (the workers' copies run concurrently)
+        self.copy_threads = int(copy_threads or max(1, min(8, (os.cpu_count() or 2) // max(1, self.worker_count))))
         self._executor = None
         self._profile_lock = threading.Lock()
         self._stage_ms = []
@@ -255,7 +267,18 @@ class PinnedStagingWeightStore(BaseWeightStore):
             # the DMA that last read this staging slot must have finished
             reuse_event.synchronize()
         target = self.staging_slots[slot_index][:unit.elements]
-        target.copy_(self.unit_source(unit))
+        source = self.unit_source(unit)
+        if _native_copy_ok(target, source):
+            # pageable -> pinned on native threads (one thread cannot reach the PCIe rate)
+            from . import _native
+
+            _native.check(
+                _native.lib().cb_host_copy(target.data_ptr(), source.data_ptr(),
+                                           source.numel() * source.element_size(), self.copy_threads),
+                "cb_host_copy",
+            )
+        else:
+            target.copy_(source)
         with self._profile_lock:
             self._stage_ms.append((time.perf_counter() - started) * 1000.0)
         return target

@@ -256,6 +256,19 @@ int cb_lm_head_topk_allgather(const void* x, const void* norm_w, float eps, cons
                               void* workspace, unsigned int* ticket, void* const* exchange, int rank,
                               int world, int slot, int slots, const int32_t* epoch, void* stream);
 
+/* -------------------------------------------------------------- host I/O */
+
+/* Host-only helpers of the weight stores (no CUDA calls; any host thread).
+ * cb_host_copy: memcpy of `bytes` split over `threads` native threads (0 =
+ * up to 16 hardware threads); replaces the single-threaded pageable ->
+ * pinned staging copy (weight_store.py:252-261). cb_read_file_ranges: n
+ * byte ranges of the file at `path` (offsets[i], sizes[i]) read with
+ * parallel pread straight into host memory dsts[i] (the safetensors tensor
+ * data -> packed arena path of weight_store.py:109-171). */
+int cb_host_copy(void* dst, const void* src, int64_t bytes, int threads);
+int cb_read_file_ranges(const char* path, int n, const int64_t* offsets, void* const* dsts, const int64_t* sizes,
+                        int threads);
+
 /* ---------------------------------------------------------------- copies */
 
 /* Host -> device copy of `bytes` on `stream` (cudaMemcpyAsync). The H2D leg
