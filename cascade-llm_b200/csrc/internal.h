@@ -39,6 +39,7 @@ int configure_smem(const char* what, void (*kernel)(KArgs...), size_t bytes) {
 int prepare_gemv();
 int prepare_attention();
 int prepare_gemm();
+int prepare_prefill_attention();
 
 // Launch `kernel<<<grid, block, smem, stream>>>(args...)` through
 // cudaLaunchKernelEx, adding the programmatic-stream-serialization attribute

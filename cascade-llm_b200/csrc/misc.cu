@@ -221,6 +221,7 @@ extern "C" int cb_prepare(void) {
   int rc = prepare_gemv();
   if (rc == kOk) rc = prepare_attention();
   if (rc == kOk) rc = prepare_gemm();
+  if (rc == kOk) rc = prepare_prefill_attention();
   return rc;
 }
 extern "C" int cb_set_error_word(int32_t* device_word) {

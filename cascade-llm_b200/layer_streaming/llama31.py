@@ -11,7 +11,8 @@ unit            reference ops (llama31.py)                             kernel (t
 qkv / q,k,v     RMSNorm :173-179, 3x F.linear :241-245, RoPE :206-212,  qkv_rope (prefill:
                 KV-cache cat :44-50                                    rmsnorm + prefill_qkv_rope)
 o_proj          repeat_kv + SDPA :182-234, F.linear + residual :246-250 attention, proj_residual
-                                                                       (prefill: gemm_residual)
+                                                                       (prefill: prefill_attention,
+                                                                       gemm_residual)
 gate_up / g,u   RMSNorm :255-263, F.linear, silu :264-271              gate_up_swiglu (gate_silu,
                                                                        up_mul for ``matrix``;
                                                                        prefill: gemm_swiglu)
@@ -343,10 +344,13 @@ class Llama31DecodeExecutor:
                     kc if wk is not None else None, vc if wv is not None else None,
                 )
         elif operation == "o_proj":
-            if splits is None:
-                splits, chunk = self.attention_config(tokens, cache.length + tokens)
-            ws = self._attention_workspace(tokens, splits)
-            ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
+            if gemm:  # prefill: causal flash attention on the tensor cores
+                ops.prefill_attention(self._q[:tokens], kc, vc, pos, self._attn[:tokens])
+            else:
+                if splits is None:
+                    splits, chunk = self.attention_config(tokens, cache.length + tokens)
+                ws = self._attention_workspace(tokens, splits)
+                ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
             wo = w("o_proj")
             if gemm:
                 ops.gemm_residual(self._attn[:tokens], wo, self._x[:tokens], self._x[:tokens])

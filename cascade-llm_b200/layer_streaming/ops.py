@@ -46,6 +46,9 @@ _SCHEMAS = {
     ),
     "position_set": "position_set(Tensor(a!) position, Tensor? src, int value) -> ()",
     "gemm_bf16": "gemm_bf16(Tensor a, Tensor w, Tensor(a!) out) -> ()",
+    "prefill_attention": (
+        "prefill_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor position, Tensor(a!) out) -> ()"
+    ),
     "gemm_residual": "gemm_residual(Tensor a, Tensor w, Tensor residual, Tensor(a!) out) -> ()",
     "gemm_swiglu": "gemm_swiglu(Tensor a, Tensor w_gate, Tensor w_up, Tensor(a!) out) -> ()",
     "gemm_partial": "gemm_partial(Tensor a, Tensor w, Tensor(a!) out) -> ()",
@@ -215,6 +218,19 @@ def attention(q, k_cache, v_cache, position, splits, chunk, out, workspace, tick
 
 def _rows(t):
     return t.numel() // t.shape[-1]
+
+
+def prefill_attention(q, k_cache, v_cache, position, out):
+    kv_heads = k_cache.shape[-3]
+    m = q.numel() // (kv_heads * 512)
+    nat.check(
+        nat.lib().cb_prefill_attention(
+            nat.ptr(q, BF16, "q"), nat.ptr(k_cache, BF16, "k_cache"), nat.ptr(v_cache, BF16, "v_cache"),
+            k_cache.shape[-2], nat.ptr(position, torch.int32, "position"), m, kv_heads,
+            nat.ptr(out, BF16, "out"), _stream(q),
+        ),
+        "cascade.prefill_attention",
+    )
 
 
 def gemm_bf16(a, w, out):

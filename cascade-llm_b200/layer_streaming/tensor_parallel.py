@@ -414,8 +414,11 @@ class TensorParallelDecoder:
             ops.qkv_rope(self._x[0], norm_in, self.eps, self._w(layer, "q_proj"), self._w(layer, "k_proj"),
                          self._w(layer, "v_proj"), self.inv_freq, pos, 0, self._q[0], kc, vc,
                          self.q_heads, self.kv_heads)
-        ws = self._attention_workspace(tokens, splits)
-        ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
+        if tokens > 1:
+            ops.prefill_attention(self._q[:tokens], kc, vc, pos, self._attn[:tokens])
+        else:
+            ws = self._attention_workspace(tokens, splits)
+            ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
         self._proj(layer, 0, self._attn, self._w(layer, "o_proj"), tokens, fused)
         if tokens > 1:
             ops.rmsnorm(self._x[:tokens], norm_post, self.eps, self._xn[:tokens])

@@ -209,6 +209,14 @@ int cb_prefill_qkv_rope(const void* xn, int M, const void* wq, const void* wk, c
                         int kv_heads, const float* inv_freq, const int32_t* position, void* q_out,
                         void* k_cache, void* v_cache, int64_t cache_len, void* stream);
 
+/* Causal GQA attention of an M-token prefill chunk on the tensor cores: the
+ * M tokens at *position .. *position+M-1 attend to the cache [0, *position +
+ * t] (token t), scale 1/sqrt(128), fp32 softmax, bf16 out. q / out: [M,
+ * 4*kv_heads, 128]; caches [kv_heads, cache_len, 128] (this step's K/V
+ * already written). Replaces llama31.py:182-234 for multi-token steps. */
+int cb_prefill_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
+                         const int32_t* position, int M, int kv_heads, void* out, void* stream);
+
 /* ------------------------------------------------------ tensor parallelism */
 
 /* Decode across N GPUs of one node (one process per GPU), an addition to the

@@ -157,3 +157,52 @@ def test_prefill_qkv_rope_matches_decode_kernel(ops, cuda, start, m, q_heads, kv
     # nothing outside the step's positions was written
     outside = torch.cat([kc[:, :start], kc[:, start + m:], vc[:, :start], vc[:, start + m:]], dim=1)
     assert bool((outside == 7.0).all())
+
+
+def _causal_reference(q, k, v, start):
+    """fp32 causal GQA attention: q [1, H, M, 128], k/v [1, KV, L, 128]; query
+    t sits at position start + t."""
+
+    groups = q.shape[1] // k.shape[1]
+    kf = k.float().repeat_interleave(groups, dim=1)
+    vf = v.float().repeat_interleave(groups, dim=1)
+    m, length = q.shape[2], k.shape[2]
+    s = q.float() @ kf.transpose(-1, -2) / (128 ** 0.5)
+    qi = torch.arange(start, start + m, device=q.device).view(-1, 1)
+    mask = torch.arange(length, device=q.device).view(1, -1) <= qi
+    s = s.masked_fill(~mask, float("-inf"))
+    return torch.softmax(s, dim=-1) @ vf
+
+
+@pytest.mark.parametrize("start,m,kv_heads", [(0, 6, 8), (0, 64, 8), (100, 5, 8), (37, 200, 2), (1000, 130, 1),
+                                              (0, 512, 8)])
+def test_prefill_attention_matches_causal_reference(ops, cuda, start, m, kv_heads):
+    length = start + m
+    cap = length + 37
+    k = randn((1, kv_heads, length, 128), 1400 + m)
+    v = randn((1, kv_heads, length, 128), 1401 + m)
+    q = randn((1, 4 * kv_heads, m, 128), 1402 + m)
+    kc = torch.full((kv_heads, cap, 128), float("nan"), dtype=BF16, device=cuda)  # past the end: never read
+    vc = torch.full_like(kc, float("nan"))
+    kc[:, :length] = k[0]
+    vc[:, :length] = v[0]
+    pos = torch.tensor([start], dtype=torch.int32, device=cuda)
+    out = torch.empty((m, 4 * kv_heads * 128), dtype=BF16, device=cuda)
+    ops.prefill_attention(q[0].transpose(0, 1).contiguous().view(m, -1), kc, vc, pos, out)
+    exact = _causal_reference(q, k, v, start)[0].transpose(0, 1).reshape(m, -1)
+    sdpa = F.scaled_dot_product_attention(
+        q, k.repeat_interleave(4, dim=1), v.repeat_interleave(4, dim=1),
+        attn_mask=(torch.arange(length, device=cuda).view(1, -1)
+                   <= torch.arange(start, length, device=cuda).view(-1, 1)))[0].transpose(0, 1).reshape(m, -1)
+    assert bool(torch.isfinite(out.float()).all())
+    torch.testing.assert_close(out.float(), sdpa.float(), rtol=2e-2, atol=2e-2)
+    # P is rounded to bf16 before PV (as the reference's bf16 SDPA does): within
+    # the bf16 SDPA's own distance from the fp32 result, plus a bf16 ulp
+    assert (out.float() - exact).abs().max() <= (sdpa.float() - exact).abs().max() + 1e-2
+    # and the split-KV decode kernel on the same step agrees
+    ws = torch.empty(ops.attention_workspace_bytes(m, 1), dtype=torch.uint8, device=cuda)
+    tickets = torch.zeros(kv_heads * m, dtype=torch.int32, device=cuda)
+    ref = torch.empty_like(out)
+    ops.attention(q[0].transpose(0, 1).contiguous().view(m, -1), kc, vc, pos, 1, -(-length // 64) * 64, ref, ws,
+                  tickets)
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
