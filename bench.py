@@ -87,7 +87,7 @@ def parse_args():
     parser.add_argument("--profile-range", action="store_true",
                         help="after warm-up, run --steps decode steps between cudaProfilerStart/Stop "
                              "(for `ncu --profile-from-start off`) and exit")
-    parser.add_argument("--micro", choices=sorted(MICRO_BYTES) + sorted(GEMM_SHAPES),
+    parser.add_argument("--micro", choices=sorted(MICRO_BYTES) + sorted(GEMM_SHAPES) + ["prefill_attention"],
                         help="time one kernel alone on a small footprint (rotating copies > L2)")
     parser.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
                         help="N>1: tensor-parallel exchange through peer memory inside the projection "
@@ -374,6 +374,43 @@ def micro_gemm(args, device):
                       "launches": launches}), flush=True)
 
 
+def micro_prefill_attention(args, device):
+    """Causal prefill attention of a --tokens chunk at the end of a --context
+    cache (8 KV heads), back to back over the caches of 8 layers: TFLOP/s
+    (QK^T and PV of the causal triangle) vs the measured dense bf16 peak."""
+
+    from layer_streaming import _native, ops
+
+    _native.check(_native.lib().cb_prepare(), "cb_prepare")
+    bf = torch.bfloat16
+    m, length = args.tokens, args.context
+    gen = torch.Generator(device=device).manual_seed(6)
+    caches = [tuple(torch.randn((8, length, 128), generator=gen, device=device).to(bf) for _ in range(2))
+              for _ in range(8)]
+    q = torch.randn((m, 32 * 128), generator=gen, device=device).to(bf)
+    out = torch.empty_like(q)
+    pos = torch.tensor([length - m], dtype=torch.int32, device=device)
+    run = lambda c: ops.prefill_attention(q, c[0], c[1], pos, out)
+    for i in range(args.warmup * 8):
+        run(caches[i % 8])
+    torch.cuda.synchronize()
+    launches = args.steps * 8
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(launches):
+        run(caches[i % 8])
+    end.record()
+    torch.cuda.synchronize()
+    us = start.elapsed_time(end) * 1000.0 / launches
+    keys = sum(length - m + t + 1 for t in range(m))  # causal (query, key) pairs per head
+    flops = 4.0 * 32 * keys * 128
+    tflops = flops / (us * 1e-6) / 1e12
+    peak, kind = measured_peak("bf16_tflops")
+    print(json.dumps({"micro": "prefill_attention", "tokens": m, "context": length, "us_per_launch": round(us, 3),
+                      "flop_per_launch": flops, "achieved_tflops": round(tflops, 1), "peak_tflops": peak,
+                      "peak_kind": kind, "frac": round(tflops / peak, 4), "launches": launches}), flush=True)
+
+
 def micro(args, device):
     """One kernel, back to back over rotating weight copies (> L2 in total)."""
 
@@ -385,6 +422,8 @@ def micro(args, device):
     name = args.micro
     if name in GEMM_SHAPES:
         return micro_gemm(args, device)
+    if name == "prefill_attention":
+        return micro_prefill_attention(args, device)
     copies = {"lm_head": 2, "gate_up": 2}.get(name, 6)
 
     def rnd(*shape, std=0.02):
