@@ -83,6 +83,9 @@ def parse_args():
     parser.add_argument("--context", type=int, default=2048)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--tokens", type=int, default=512, help="rows of the --micro gemm_* cases")
+    parser.add_argument("--sweep", action="store_true",
+                        help="BASELINE config 3: each projection at M in {1, 6, 64, 512}, HBM-resident and "
+                             "H2D-streamed through two slots (one JSON line per case)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--profile-range", action="store_true",
                         help="after warm-up, run --steps decode steps between cudaProfilerStart/Stop "
@@ -258,6 +261,30 @@ def time_e2e(executor, runtime, token, steps):
             "d2h_bytes_per_step": d2h}
 
 
+def time_streamed(plan, store, resident, executor, device, token, steps=3):
+    """The reference's own mode on this GPU: every decode token streams the 15 GB
+    of layer weights H2D from the pinned host arena through two 224 MiB slots
+    (copy stream overlapped with the compute stream), same kernels."""
+
+    import layer_streaming as ls
+
+    runtime = ls.DoubleBufferRuntime(plan, store, resident, device, weights="streamed", profile=True)
+    with torch.inference_mode():
+        token = step(executor, runtime, token).topk_indices[..., 0]  # warm-up
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            token = step(executor, runtime, token).topk_indices[..., 0]
+        end.record()
+        torch.cuda.synchronize()
+    profile = runtime.last_profile or {}
+    return {"ms_per_token": round(start.elapsed_time(end) / steps, 2), "steps": steps,
+            "h2d_bytes_per_token": int(profile.get("h2d_bytes", plan.stream_bytes_per_token)),
+            "h2d_effective_gbps": round(float(profile.get("h2d_effective_gbps", 0.0)), 2),
+            "note": "weights='streamed': H2D-bound (PCIe); the timed value is the HBM-resident mode"}
+
+
 def time_gate_up(executor, runtime, plan, reps=4):
     """Live timing of the dominant kernel: the 32 gate+up GEMVs back to back
     (one per layer, so the 7.5 GB they read cannot come from L2)."""
@@ -411,6 +438,99 @@ def micro_prefill_attention(args, device):
                       "peak_kind": kind, "frac": round(tflops / peak, 4), "launches": launches}), flush=True)
 
 
+def sweep(args, device):
+    """Matrix-group projections (QKV + RoPE, O + residual, gate+up + SwiGLU,
+    down + residual) at M rows (GEMV kernel for M = 1, tcgen05 GEMM above):
+    HBM-resident over 8 rotating weight copies (> L2), and H2D-streamed from
+    pinned host memory through two device slots (copy stream overlapped with
+    the compute stream), as the reference's runtime streams its units."""
+
+    from layer_streaming import _native, ops
+
+    _native.check(_native.lib().cb_prepare(), "cb_prepare")
+    bf = torch.bfloat16
+    gen = torch.Generator(device=device).manual_seed(9)
+    rnd = lambda *shape: (torch.randn(shape, generator=gen, device=device) * 0.02).to(bf)
+    shapes = {"qkv": [(4096, 4096), (1024, 4096), (1024, 4096)], "o_proj": [(4096, 4096)],
+              "gate_up": [(14336, 4096), (14336, 4096)], "down_proj": [(4096, 14336)]}
+    inv = torch.ones(64, device=device)
+    pos = torch.zeros(1, dtype=torch.int32, device=device)
+    kc = torch.zeros((8, 600, 128), dtype=bf, device=device)
+    vc = torch.zeros_like(kc)
+    for name, mats in shapes.items():
+        k_in = mats[0][1]
+        x = (torch.randn((512, k_in), generator=gen, device=device)).to(bf)
+        res = torch.randn((512, 4096), generator=gen, device=device).to(bf)
+        q = torch.empty((512, 4096), dtype=bf, device=device)
+        mlp = torch.empty((512, 14336), dtype=bf, device=device)
+
+        def run(w, m, name=name, x=x, res=res, q=q, mlp=mlp):
+            if name == "qkv":
+                if m == 1:
+                    ops.qkv_rope(x[0], None, 1e-5, w[0], w[1], w[2], inv, pos, 0, q[0], kc, vc)
+                else:
+                    ops.prefill_qkv_rope(x[:m], w[0], w[1], w[2], inv, pos, q[:m], kc, vc)
+            elif name == "gate_up":
+                if m == 1:
+                    ops.gate_up_swiglu(x[0], None, 1e-5, w[0], w[1], mlp[0])
+                else:
+                    ops.gemm_swiglu(x[:m], w[0], w[1], mlp[:m])
+            elif m == 1:
+                ops.proj_residual(x[0], w[0], res[0], res[0])
+            else:
+                ops.gemm_residual(x[:m], w[0], res[:m], res[:m])
+
+        copies = [[rnd(*s) for s in mats] for _ in range(8)]
+        host = [torch.empty(s, dtype=bf).pin_memory() for s in mats]
+        for h, d in zip(host, copies[0]):
+            h.copy_(d.cpu())
+        slots = [[torch.empty(s, dtype=bf, device=device) for s in mats] for _ in range(2)]
+        nbytes = sum(a * b * 2 for a, b in mats)
+        flop_per_row = 2 * sum(a * b for a, b in mats)
+        copy_stream = torch.cuda.Stream(device)
+        for m in (1, 6, 64, 512):
+            for i in range(16):
+                run(copies[i % 8], m)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(32):
+                run(copies[i % 8], m)
+            e1.record()
+            torch.cuda.synchronize()
+            resident_us = e0.elapsed_time(e1) * 1000.0 / 32
+            # streamed: unit i is copied into slot i % 2 while unit i - 1 computes
+            ready = [torch.cuda.Event() for _ in range(2)]
+            free = [torch.cuda.Event() for _ in range(2)]
+            compute = torch.cuda.current_stream(device)
+            for f in free:
+                f.record(compute)
+            torch.cuda.synchronize()
+            started = time.perf_counter()
+            n = 16
+            for i in range(n):
+                sl = i % 2
+                with torch.cuda.stream(copy_stream):
+                    copy_stream.wait_event(free[sl])
+                    for h, d in zip(host, slots[sl]):
+                        ops.memcpy_h2d_async(d, h)
+                    ready[sl].record(copy_stream)
+                compute.wait_event(ready[sl])
+                run(slots[sl], m)
+                free[sl].record(compute)
+            torch.cuda.synchronize()
+            streamed_us = (time.perf_counter() - started) * 1e6 / n
+            print(json.dumps({
+                "sweep": name, "M": m, "weight_bytes": nbytes,
+                "resident_us": round(resident_us, 2),
+                "resident_gbs": round(nbytes / (resident_us * 1e-6) / 1e9, 1),
+                "resident_tflops": round(flop_per_row * m / (resident_us * 1e-6) / 1e12, 1),
+                "streamed_us": round(streamed_us, 2),
+                "streamed_h2d_gbs": round(nbytes / (streamed_us * 1e-6) / 1e9, 2),
+            }), flush=True)
+        del copies, host, slots
+
+
 def micro(args, device):
     """One kernel, back to back over rotating weight copies (> L2 in total)."""
 
@@ -545,7 +665,7 @@ def tensor_parallel(args, world, rank, local, device):
 
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     weights = TensorParallelWeights.seeded(world, rank, device, seed=0)
-    extra = args.warmup + args.steps * 2 + 64
+    extra = args.warmup + args.steps * 2 + 72
     decoder = TensorParallelDecoder(Config(), weights, top_k=10, max_length=args.context + extra,
                                     exchange=args.exchange)
     ids = random_ids(args.context, seed=1).to(device)
@@ -688,6 +808,9 @@ def main():
     if args.micro:
         micro(args, device)
         return
+    if args.sweep:
+        sweep(args, device)
+        return
     if world > 1:
         tensor_parallel(args, world, rank, local, device)
         return
@@ -695,7 +818,7 @@ def main():
     def barrier():
         pass
 
-    extra = args.warmup + args.steps * 2 + 64
+    extra = args.warmup + args.steps * 2 + 72
     plan, store, resident, runtime, executor = build_engine(device, args.context, extra)
     token, prefill_ms = prefill(executor, runtime, device, args.context)
     if args.profile_range:
@@ -717,6 +840,7 @@ def main():
     executor.check_errors()
     e2e = time_e2e(executor, runtime, token, args.steps)
     gate_up_ms = time_gate_up(executor, runtime, plan)
+    streamed = time_streamed(plan, store, resident, executor, device, token)
     peak, peak_kind = measured_peak()
     context = executor.kv_cache.length - args.steps - 1  # mean cached length over the timed steps
     achieved = GATE_UP_BYTES / (gate_up_ms / 1000.0) / 1e9
@@ -758,6 +882,7 @@ def main():
             "frac_of_8tbs": round(step_gbs / 8000.0, 4), "bytes_per_token": step_bytes(context),
         },
         "cpu_baseline": baseline,
+        "streamed_mode": streamed,
         "prefill": {
             "tokens": args.context, "chunk": 512, "ms": round(prefill_ms, 2),
             "tokens_per_s": round(args.context / (prefill_ms / 1000.0), 1),
