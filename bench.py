@@ -641,8 +641,8 @@ def reference_arm(args, rank):
     return {
         "metric": METRIC, "value": round(value, 3), "unit": "ms/token", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded random-init weights, random token ids)",
+        "higher_is_better": False, "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded random-init weights, random token ids)",
         "config": {"workload": "llama31-8b decode bs=1, {}-token context".format(args.context),
                    "context": args.context, "flush": "weights (16 GB) larger than L2"},
         "impl": "reference",

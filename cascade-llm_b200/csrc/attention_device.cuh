@@ -209,8 +209,12 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, co
   }
   float acc[2] = {0.f, 0.f};
   const int e0 = tid, e1 = tid + kAttnConsumers;  // outputs (h, d) = e / 128, e % 128
-  for (int base = 0; base < p.splits; base += 256) {
-    const int nb = min(256, p.splits - base);
+  // splits that start past this token's last visible position hold no keys
+  // (weight 0): only the first `live` take part
+  const int64_t visible = min(int64_t(__ldcg(p.pos)) + m + 1, p.cache_len);
+  const int live = max(1, min(p.splits, int((visible + p.chunk - 1) / p.chunk)));
+  for (int base = 0; base < live; base += 256) {
+    const int nb = min(256, live - base);
     sync();
     for (int i = tid; i < kGroup * nb; i += kAttnConsumers) {
       const int h = i / nb, j = i % nb;
