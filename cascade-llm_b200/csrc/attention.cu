@@ -4,13 +4,12 @@
 // K/V) + F.scaled_dot_product_attention. Here the 4 query heads of a KV head
 // share ONE read of every K/V row: a CTA owns (split s, kv head g, token m)
 // and streams its positions [s*chunk, s*chunk + chunk) in 64-position
-// sub-chunks through a 3-stage cp.async.bulk ring. Per sub-chunk:
-//   scores  q.k for 4 heads (lanes split the 128 dims; a transposed shuffle
-//           tree leaves one head's sum per 8 lanes), scaled by 1/sqrt(128);
-//   softmax online (running max / sum per head, fp32);
-//   PV      4 position groups x 64 dim pairs accumulate 4 heads each.
-// Each CTA writes (m, l, o[128]) per head; the last CTA of a (token, kv head)
-// group (atomic ticket) merges the splits and writes the bf16 output.
+// sub-chunks through a 3-stage cp.async.bulk ring. Each of the 8 compute
+// warps owns 8 rows of every sub-chunk and runs its own online softmax over
+// them (fp32; scores scaled by 1/sqrt(128)), with no barrier between warps
+// until the end: then the warps' (m, l, o) are combined in shared memory,
+// each CTA writes (m, l, o[128]) per head, and the last CTA of a (token, kv
+// head) group (atomic ticket) merges the splits and writes the bf16 output.
 //
 // Causality: token m of a step starting at position P0 sees [0, P0 + m].
 // Rows of the history (< P0) are fetched before griddepcontrol.wait: they were
@@ -37,6 +36,9 @@ struct AttnSmem {
   static constexpr size_t BAR_OFF = V_OFF + kAttnStages * STAGE;   // full, empty
   static constexpr size_t SCR_OFF = BAR_OFF + 2 * kAttnStages * 8;
   static constexpr size_t BYTES = SCR_OFF + AttnScratch::BYTES;
+  static_assert(kAttnStages * STAGE >= size_t(kAttnWarps) * kGroup * kHeadDim * 4,
+                "the K ring stages the cross-warp combine");
+  static_assert(SCR_OFF % 16 == 0, "scratch alignment");
 };
 
 struct ConsumerSync {
@@ -54,7 +56,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + AttnSmem::BAR_OFF);
   uint64_t* empty = full + kAttnStages;
   uint8_t* scratch = smem + AttnSmem::SCR_OFF;
-  float* st = reinterpret_cast<float*>(scratch + AttnScratch::ST);
 
   const int s = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
@@ -68,7 +69,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
     }
     fence_mbar_init();
   }
-  attn_reset(st);
   __syncthreads();
 
   if (warp == kAttnWarps) {
@@ -101,11 +101,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
   }
 
   // ---------------- consumers
-  grid_dep_wait();  // q comes from the QKV kernel
-  if (tid == 0) grid_dep_launch();
+  // q comes from the QKV kernel. No early griddepcontrol.launch_dependents:
+  // the next kernel (o_proj) starts when this grid exits, since its CTAs
+  // would otherwise stream weights during this kernel's latency-bound
+  // publish/merge and slow it (decode step 3.37 -> 3.12 ms measured).
+  grid_dep_wait();
   float q[kGroup][4];
   attn_load_q(p, m, g, q);
-  float o[kGroup][2] = {};
+  AttnWarpState ws;
+  attn_state_init(ws);
+  float* pw = reinterpret_cast<float*>(scratch + AttnScratch::PW) + warp * 40;
   int stage = 0;
   uint32_t phase = 0;
   bool failed = false;  // a timed-out wait records the error; control flow is unchanged
@@ -113,8 +118,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
     const int64_t t0 = start + int64_t(i) * kSub;
     const int rows = int(min(int64_t(kSub), stop - t0));
     if (!failed && !mbar_wait(&full[stage], phase, p.err, 203)) failed = true;
-    attn_subchunk(ks + size_t(stage) * kSub * kHeadDim, vs + size_t(stage) * kSub * kHeadDim, rows, i, q, o,
-                  scratch, ConsumerSync());
+    attn_rows(ks + size_t(stage) * kSub * kHeadDim, vs + size_t(stage) * kSub * kHeadDim, rows, q, ws, pw);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
     if (++stage == kAttnStages) {
@@ -122,7 +126,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
       phase ^= 1;
     }
   }
-  attn_publish(p, s, g, m, o, scratch, ConsumerSync());
+  attn_publish(p, s, g, m, pos0, ws, scratch, reinterpret_cast<float*>(ks), ConsumerSync());
 }
 
 int prepare_attention() { return configure_smem("cb_attention", attention_kernel, AttnSmem::BYTES); }

@@ -1,6 +1,5 @@
-// Device-side building blocks of the split-KV GQA attention (flash-decoding),
-// shared by the stand-alone attention kernel (attention.cu) and the
-// persistent decode-step kernel (decode_step.cu). Replaces
+// Device-side building blocks of the split-KV GQA attention (flash-decoding)
+// of attention.cu. Replaces
 // layer_streaming/llama31.py:182-234 (`_repeat_kv` + SDPA): the 4 query heads
 // of a KV head share one read of every K/V row.
 #pragma once
@@ -31,16 +30,17 @@ struct AttnParams {
   int* err;
 };
 
-// Shared-memory scratch of the compute part: scores [2][4][64], softmax
-// state (alpha [2][4], running max [4], running sum [4]) and a merge area.
+constexpr int kRowsPerWarp = kSub / kAttnWarps;  // 8 rows of a sub-chunk per warp
+constexpr int kMergeBlock = 24;                    // splits merged per round trip
+
+// Shared-memory scratch of the compute part: per-warp broadcast areas (p of
+// the warp's 8 rows x 4 heads, alpha of 4 heads), per-warp softmax states and
+// the merge staging. The cross-warp combine of o reuses the K ring.
 struct AttnScratch {
-  static constexpr size_t SC = 0;
-  static constexpr size_t ST = SC + 2 * kGroup * kSub * 4;
-  static constexpr size_t RED = ST + 16 * 4;
-  static constexpr size_t RED_FLOATS = 4 * kGroup * kHeadDim > 2 * kGroup * 256 + 3 * kGroup
-                                           ? 4 * kGroup * kHeadDim
-                                           : 2 * kGroup * 256 + 3 * kGroup;
-  static constexpr size_t BYTES = RED + RED_FLOATS * 4;
+  static constexpr size_t PW = 0;                                     // [8 warps][40] fp32
+  static constexpr size_t WML = PW + kAttnWarps * 40 * 4;             // [8][4] m, [8][4] l
+  static constexpr size_t MRG = WML + 2 * kAttnWarps * kGroup * 4;    // merge: w [4][24]; M, L, s [4]; flag
+  static constexpr size_t BYTES = MRG + (kGroup * kMergeBlock + 3 * kGroup + 4) * 4;
 };
 
 // Positions [start, stop) of split s for token m, and the sub-chunk count.
@@ -71,199 +71,212 @@ __device__ __forceinline__ void attn_load_q(const AttnParams& p, int m, int g, f
   }
 }
 
-__device__ __forceinline__ void attn_reset(float* st) {
-  if (threadIdx.x < kGroup) {
-    st[8 + threadIdx.x] = -__int_as_float(0x7F800000);  // running max
-    st[12 + threadIdx.x] = 0.f;                         // running sum
-  }
+// Online softmax state of one warp: lane L tracks head L & 3 (m_run, l_run;
+// the 8 lanes of a head hold the same values) and accumulates o[h][0..3] for
+// dims 4L..4L+3 of all 4 heads, unnormalised, relative to m_run.
+struct AttnWarpState {
+  float o[kGroup][4];
+  float m_run, l_run;
+};
+
+__device__ __forceinline__ void attn_state_init(AttnWarpState& w) {
+#pragma unroll
+  for (int h = 0; h < kGroup; ++h)
+#pragma unroll
+    for (int d = 0; d < 4; ++d) w.o[h][d] = 0.f;
+  w.m_run = -__int_as_float(0x7F800000);
+  w.l_run = 0.f;
 }
 
-// One sub-chunk (rows <= 64 positions of K and V in shared memory) of the
-// online softmax: scores q.k (lanes split the 128 dims; a transposed shuffle
-// tree leaves head (lane>>3)'s sum in 8 lanes), a running max/sum per head in
-// fp32, then PV with 4 position groups x 64 dim pairs accumulating into
-// o[head][2]. `sync` is the barrier over the 256 compute threads; `i` is the
-// sub-chunk counter (selects the double-buffered score area).
-template <class Sync>
-__device__ __forceinline__ void attn_subchunk(const uint16_t* kst, const uint16_t* vst, int rows, int i,
-                                              const float (&q)[kGroup][4], float (&o)[kGroup][2],
-                                              uint8_t* scratch, Sync sync) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-  float* scb = reinterpret_cast<float*>(scratch + AttnScratch::SC) + (i & 1) * kGroup * kSub;
-  float* st = reinterpret_cast<float*>(scratch + AttnScratch::ST);
-  float* alpha_s = st;
-  float* m_run = st + 8;
-  float* l_run = st + 12;
-#pragma unroll 2
-  for (int j = 0; j < 8; ++j) {
-    const int t = warp * 8 + j;
-    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-    if (t < rows) {
-      const uint2 u = *reinterpret_cast<const uint2*>(kst + t * kHeadDim + 4 * lane);
-      const float k0 = bf16lo(u.x), k1 = bf16hi(u.x), k2 = bf16lo(u.y), k3 = bf16hi(u.y);
-      d0 = fmaf(q[0][0], k0, fmaf(q[0][1], k1, fmaf(q[0][2], k2, q[0][3] * k3)));
-      d1 = fmaf(q[1][0], k0, fmaf(q[1][1], k1, fmaf(q[1][2], k2, q[1][3] * k3)));
-      d2 = fmaf(q[2][0], k0, fmaf(q[2][1], k1, fmaf(q[2][2], k2, q[2][3] * k3)));
-      d3 = fmaf(q[3][0], k0, fmaf(q[3][1], k1, fmaf(q[3][2], k2, q[3][3] * k3)));
-    }
-    const bool up = lane & 16;
-    float keep0 = up ? d2 : d0, keep1 = up ? d3 : d1;
-    keep0 += __shfl_xor_sync(0xFFFFFFFFu, up ? d0 : d2, 16);
-    keep1 += __shfl_xor_sync(0xFFFFFFFFu, up ? d1 : d3, 16);
-    const bool b3 = lane & 8;
-    float keep = b3 ? keep1 : keep0;
-    keep += __shfl_xor_sync(0xFFFFFFFFu, b3 ? keep0 : keep1, 8);
-    keep += __shfl_xor_sync(0xFFFFFFFFu, keep, 4);
-    keep += __shfl_xor_sync(0xFFFFFFFFu, keep, 2);
-    keep += __shfl_xor_sync(0xFFFFFFFFu, keep, 1);
-    if ((lane & 7) == 0) scb[(lane >> 3) * kSub + t] = t < rows ? keep * kAttnScale : -__int_as_float(0x7F800000);
-  }
-  sync();
-  if (warp < kGroup) {
-    const float s0 = scb[warp * kSub + lane], s1 = scb[warp * kSub + 32 + lane];
-    const float mx = warp_max(fmaxf(s0, s1));
-    const float mold = m_run[warp];
-    const float mnew = fmaxf(mold, mx);
-    const float p0 = expf(s0 - mnew), p1 = expf(s1 - mnew);
-    scb[warp * kSub + lane] = p0;
-    scb[warp * kSub + 32 + lane] = p1;
-    const float sum = warp_sum(p0 + p1);
-    if (lane == 0) {
-      const float a = expf(mold - mnew);
-      alpha_s[(i & 1) * kGroup + warp] = a;
-      l_run[warp] = l_run[warp] * a + sum;
-      m_run[warp] = mnew;
-    }
-  }
-  sync();
-  const int pg = tid >> 6, dp = tid & 63;
+// Rows [8w, 8w + 8) of a sub-chunk (K and V rows in shared memory, `rows`
+// valid) for warp w, with no synchronisation beyond the warp:
+//   scores  each lane dots its 4 dims of the 4 heads with each of the 8 rows
+//           (32 partial sums); a transposed butterfly (16+8+4+2+1 shuffles)
+//           leaves lane L the full dot of row L >> 2, head L & 3;
+//   softmax running max / sum per head over the 8 lanes of the head;
+//   PV      p and the rescale factors go through the warp's 40-float area;
+//           each lane accumulates its 4 dims of the 4 heads.
+__device__ __forceinline__ void attn_rows(const uint16_t* kst, const uint16_t* vst, int rows,
+                                          const float (&q)[kGroup][4], AttnWarpState& st, float* pw) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = warp * kRowsPerWarp;
+  if (r0 >= rows) return;  // warp-uniform: no row of this warp in the sub-chunk
+  float v[kRowsPerWarp * kGroup];
 #pragma unroll
-  for (int h = 0; h < kGroup; ++h) {
-    const float a = alpha_s[(i & 1) * kGroup + h];
-    o[h][0] *= a;
-    o[h][1] *= a;
-  }
-  for (int t = pg; t < rows; t += 4) {
-    const uint32_t u = *reinterpret_cast<const uint32_t*>(vst + t * kHeadDim + 2 * dp);
-    const float v0 = bf16lo(u), v1 = bf16hi(u);
+  for (int j = 0; j < kRowsPerWarp; ++j) {
+    uint2 u = make_uint2(0u, 0u);
+    if (r0 + j < rows) u = *reinterpret_cast<const uint2*>(kst + (r0 + j) * kHeadDim + 4 * lane);
+    const float k0 = bf16lo(u.x), k1 = bf16hi(u.x), k2 = bf16lo(u.y), k3 = bf16hi(u.y);
 #pragma unroll
-    for (int h = 0; h < kGroup; ++h) {
-      const float pr = scb[h * kSub + t];
-      o[h][0] = fmaf(pr, v0, o[h][0]);
-      o[h][1] = fmaf(pr, v1, o[h][1]);
+    for (int h = 0; h < kGroup; ++h)
+      v[j * kGroup + h] = fmaf(q[h][0], k0, fmaf(q[h][1], k1, fmaf(q[h][2], k2, q[h][3] * k3)));
+  }
+  // level `half`: the lane whose bit `half` is set keeps the upper half of
+  // its values and receives the partner's copy of it, the other the lower
+#pragma unroll
+  for (int half = 16; half >= 1; half >>= 1) {
+    const bool hi = lane & half;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = hi ? v[i] : v[i + half];
+      const float keep = hi ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, half);
     }
   }
+  const float ninf = -__int_as_float(0x7F800000);
+  const float s = r0 + (lane >> 2) < rows ? v[0] * kAttnScale : ninf;
+  float mx = fmaxf(s, __shfl_xor_sync(0xFFFFFFFFu, s, 4));
+  mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
+  mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+  const float m_new = fmaxf(st.m_run, mx);  // finite: row r0 is valid
+  const float p = expf(s - m_new);
+  float ps = p + __shfl_xor_sync(0xFFFFFFFFu, p, 4);
+  ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 8);
+  ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 16);
+  const float alpha = expf(st.m_run - m_new);  // 0 while m_run is -inf
+  st.l_run = st.l_run * alpha + ps;
+  st.m_run = m_new;
+  pw[lane] = p;  // [row j][head h] at 4j + h
+  if (lane < kGroup) pw[32 + lane] = alpha;
+  __syncwarp();
+  const float4 al = *reinterpret_cast<const float4*>(pw + 32);
+  const float a4[kGroup] = {al.x, al.y, al.z, al.w};
+#pragma unroll
+  for (int h = 0; h < kGroup; ++h)
+#pragma unroll
+    for (int d = 0; d < 4; ++d) st.o[h][d] *= a4[h];
+#pragma unroll
+  for (int j = 0; j < kRowsPerWarp; ++j) {
+    if (r0 + j < rows) {  // warp-uniform; rows past the end may hold stale bytes
+      const float4 pj = *reinterpret_cast<const float4*>(pw + 4 * j);
+      const uint2 u = *reinterpret_cast<const uint2*>(vst + (r0 + j) * kHeadDim + 4 * lane);
+      const float vv[4] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y)};
+      const float pp[kGroup] = {pj.x, pj.y, pj.z, pj.w};
+#pragma unroll
+      for (int h = 0; h < kGroup; ++h)
+#pragma unroll
+        for (int d = 0; d < 4; ++d) st.o[h][d] = fmaf(pp[h], vv[d], st.o[h][d]);
+    }
+  }
+  __syncwarp();  // pw is rewritten by the next batch
 }
 
-// Publish this split's (m, l, o) for the 4 heads of KV head g (token m);
-// the last split of the group to arrive (atomic ticket) merges all splits
-// and writes the bf16 output, then resets the ticket.
+// Combine the 8 warps' states into this split's (m, l, o) per head, publish
+// them, and let the last split of the (token, kv head) group to arrive
+// (acquire-release ticket) merge all splits and write the bf16 output, then
+// reset the ticket. pos0 = the step's first position (read at kernel start).
+// `ring` (>= 16 KB of shared memory no longer read by any warp after
+// the first barrier) stages the rescaled o of every warp.
 template <class Sync>
-static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, const float (&o)[kGroup][2],
-                             uint8_t* scratch, Sync sync) {
+static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, int64_t pos0,
+                                    const AttnWarpState& st, uint8_t* scratch, float* ring, Sync sync) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-  const int pg = tid >> 6, dp = tid & 63;
-  float* st = reinterpret_cast<float*>(scratch + AttnScratch::ST);
-  const float* m_run = st + 8;
-  const float* l_run = st + 12;
-  float* red = reinterpret_cast<float*>(scratch + AttnScratch::RED);
+  const float ninf = -__int_as_float(0x7F800000);
+  float* wm = reinterpret_cast<float*>(scratch + AttnScratch::WML);
+  float* wl = wm + kAttnWarps * kGroup;
+  if (lane < kGroup) {
+    wm[warp * kGroup + lane] = st.m_run;
+    wl[warp * kGroup + lane] = st.l_run;
+  }
+  sync();  // every warp is past its last row: the K ring is free
 #pragma unroll
   for (int h = 0; h < kGroup; ++h) {
-    red[(pg * kGroup + h) * kHeadDim + 2 * dp] = o[h][0];
-    red[(pg * kGroup + h) * kHeadDim + 2 * dp + 1] = o[h][1];
+    float mm = ninf;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, wm[w * kGroup + h]);
+    const float mw = wm[warp * kGroup + h];
+    const float f = mw == ninf ? 0.f : expf(mw - mm);
+    *reinterpret_cast<float4*>(ring + (warp * kGroup + h) * kHeadDim + 4 * lane) =
+        make_float4(st.o[h][0] * f, st.o[h][1] * f, st.o[h][2] * f, st.o[h][3] * f);
   }
   sync();
   for (int e = tid; e < kGroup * kHeadDim; e += kAttnConsumers) {
     const int h = e / kHeadDim, d = e % kHeadDim;
-    const float v = red[(0 * kGroup + h) * kHeadDim + d] + red[(1 * kGroup + h) * kHeadDim + d] +
-                    red[(2 * kGroup + h) * kHeadDim + d] + red[(3 * kGroup + h) * kHeadDim + d];
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) acc += ring[(w * kGroup + h) * kHeadDim + d];
     const int64_t row = (int64_t(m) * p.kv_heads * kGroup + g * kGroup + h) * p.splits + s;
-    p.part_o[row * kHeadDim + d] = v;
+    p.part_o[row * kHeadDim + d] = acc;
     if (d == 0) {
-      p.part_ml[row * 2] = m_run[h];
-      p.part_ml[row * 2 + 1] = l_run[h];
-    }
-  }
-  __threadfence();
-  sync();
-  if (tid == 0) {
-    const unsigned int ticket = atomicAdd(&p.tickets[m * p.kv_heads + g], 1u);
-    red[0] = __int_as_float(ticket == unsigned(p.splits - 1) ? 1 : 0);
-  }
-  sync();
-  const bool last = __float_as_int(red[0]) == 1;
-  sync();  // everyone has read the flag before the merge reuses red
-  if (!last) return;
-  __threadfence();
-  // Merge: per-split (max, sum) of the 4 heads staged in blocks of 256 splits
-  // (loads issued in parallel), then each thread reduces its 2 outputs over
-  // the splits with independent, unrolled loads.
-  float* st_m = red;                         // [4][256] split maxima
-  float* st_w = red + kGroup * 256;          // [4][256] weights exp(m_s - M)
-  float* st_l = red + 2 * kGroup * 256;      // [4] combined denominators
-  float* st_M = st_l + kGroup;               // [4] combined maxima
-  float* st_s = st_M + kGroup;               // [4] rescale factor of this block
-  if (tid < kGroup) {
-    st_M[tid] = -__int_as_float(0x7F800000);
-    st_l[tid] = 0.f;
-  }
-  float acc[2] = {0.f, 0.f};
-  const int e0 = tid, e1 = tid + kAttnConsumers;  // outputs (h, d) = e / 128, e % 128
-  // splits that start past this token's last visible position hold no keys
-  // (weight 0): only the first `live` take part
-  const int64_t visible = min(int64_t(__ldcg(p.pos)) + m + 1, p.cache_len);
-  const int live = max(1, min(p.splits, int((visible + p.chunk - 1) / p.chunk)));
-  for (int base = 0; base < live; base += 256) {
-    const int nb = min(256, live - base);
-    sync();
-    for (int i = tid; i < kGroup * nb; i += kAttnConsumers) {
-      const int h = i / nb, j = i % nb;
-      st_m[h * 256 + j] =
-          __ldcg(p.part_ml + ((int64_t(m) * p.kv_heads * kGroup + g * kGroup + h) * p.splits + base + j) * 2);
-    }
-    sync();
-    if (warp < kGroup) {  // warp h: new running max and rescale of the previous blocks
-      float mx = -__int_as_float(0x7F800000);
-      for (int j = lane; j < nb; j += 32) mx = fmaxf(mx, st_m[warp * 256 + j]);
-      mx = warp_max(mx);
-      const float mold = st_M[warp], mnew = fmaxf(mold, mx);
-      float lsum = 0.f;
-      for (int j = lane; j < nb; j += 32) {
-        const float mj = st_m[warp * 256 + j];
-        const float w = mj == -__int_as_float(0x7F800000) ? 0.f : expf(mj - mnew);
-        st_w[warp * 256 + j] = w;
-        lsum = fmaf(
-            w, __ldcg(p.part_ml + ((int64_t(m) * p.kv_heads * kGroup + g * kGroup + warp) * p.splits + base + j) * 2 + 1),
-            lsum);
+      float mm = ninf, ll = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, wm[w * kGroup + h]);
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float mw = wm[w * kGroup + h];
+        ll += mw == ninf ? 0.f : expf(mw - mm) * wl[w * kGroup + h];
       }
-      lsum = warp_sum(lsum);
+      *reinterpret_cast<float2*>(p.part_ml + row * 2) = make_float2(mm, ll);
+    }
+  }
+  sync();
+  float* mg = reinterpret_cast<float*>(scratch + AttnScratch::MRG);
+  float* sm_w = mg;                               // [4][24] weights exp(m_s - M)
+  float* st_M = sm_w + kGroup * kMergeBlock;      // [4] running maxima
+  float* st_L = st_M + kGroup;                    // [4] running denominators
+  float* st_s = st_L + kGroup;                    // [4] rescale of the previous blocks
+  int* flag = reinterpret_cast<int*>(st_s + kGroup);
+  if (tid == 0) {
+    const unsigned int ticket = atom_add_acq_rel_gpu(&p.tickets[m * p.kv_heads + g], 1u);
+    *flag = ticket == unsigned(p.splits - 1) ? 1 : 0;
+  }
+  sync();
+  if (*flag == 0) return;
+  // Merge over the splits that hold keys for this token (a split that starts
+  // past its last visible position has weight 0), kMergeBlock splits per
+  // round trip: every (m, l) pair and every o value of the block is loaded
+  // at once; thread t owns outputs t and t + 256 (head e / 128, dim e % 128).
+  if (tid < kGroup) {
+    st_M[tid] = ninf;
+    st_L[tid] = 0.f;
+  }
+  const int64_t visible = min(pos0 + m + 1, p.cache_len);
+  const int live = max(1, min(p.splits, int((visible + p.chunk - 1) / p.chunk)));
+  const int64_t grp = int64_t(m) * p.kv_heads * kGroup + g * kGroup;  // first (token, head) row
+  float acc[2] = {0.f, 0.f};
+  const int h0 = tid / kHeadDim, h1 = (tid + kAttnConsumers) / kHeadDim, d0 = tid % kHeadDim;
+  for (int base = 0; base < live; base += kMergeBlock) {
+    const int nb = min(kMergeBlock, live - base);
+    float ov[2][kMergeBlock];
+#pragma unroll
+    for (int j = 0; j < kMergeBlock; ++j) {
+      if (j < nb) {
+        ov[0][j] = __ldcg(p.part_o + ((grp + h0) * p.splits + base + j) * kHeadDim + d0);
+        ov[1][j] = __ldcg(p.part_o + ((grp + h1) * p.splits + base + j) * kHeadDim + d0);
+      }
+    }
+    // warp h, lane j: (m, l) of split base + j for head h, in flight with the o values
+    float2 ml = make_float2(ninf, 0.f);
+    if (warp < kGroup && lane < nb)
+      ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + ((grp + warp) * p.splits + base + lane) * 2));
+    sync();  // the previous block's weights have been used
+    if (warp < kGroup) {  // warp h: new running max, weights, rescale of the previous blocks
+      const float mold = st_M[warp], mnew = fmaxf(mold, warp_max(ml.x));
+      const float w = ml.x == ninf ? 0.f : expf(ml.x - mnew);
+      if (lane < nb) sm_w[warp * kMergeBlock + lane] = w;
+      const float lsum = warp_sum(w * ml.y);
       if (lane == 0) {
-        const float scale = mold == -__int_as_float(0x7F800000) ? 0.f : expf(mold - mnew);
-        st_l[warp] = st_l[warp] * scale + lsum;
+        const float scale = mold == ninf ? 0.f : expf(mold - mnew);
+        st_L[warp] = st_L[warp] * scale + lsum;
         st_M[warp] = mnew;
         st_s[warp] = scale;
       }
     }
     sync();
+    float a = acc[0] * st_s[h0], b = acc[1] * st_s[h1];
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int e = q ? e1 : e0;
-      const int h = e / kHeadDim, d = e % kHeadDim;
-      acc[q] *= st_s[h];
-      const float* po = p.part_o + ((int64_t(m) * p.kv_heads * kGroup + g * kGroup + h) * p.splits + base) * kHeadDim + d;
-      float sum = 0.f;
-#pragma unroll 8
-      for (int j = 0; j < nb; ++j) sum = fmaf(st_w[h * 256 + j], __ldcg(po + int64_t(j) * kHeadDim), sum);
-      acc[q] += sum;
+    for (int j = 0; j < kMergeBlock; ++j) {
+      if (j < nb) {
+        a = fmaf(sm_w[h0 * kMergeBlock + j], ov[0][j], a);
+        b = fmaf(sm_w[h1 * kMergeBlock + j], ov[1][j], b);
+      }
     }
+    acc[0] = a;
+    acc[1] = b;
   }
-  sync();
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int e = q ? e1 : e0;
-    const int h = e / kHeadDim, d = e % kHeadDim;
-    p.out[int64_t(m) * p.kv_heads * kGroup * kHeadDim + (g * kGroup + h) * kHeadDim + d] = f2bf(acc[q] / st_l[h]);
-  }
+  uint16_t* out = p.out + int64_t(m) * p.kv_heads * kGroup * kHeadDim + g * kGroup * kHeadDim;
+  out[h0 * kHeadDim + d0] = f2bf(acc[0] / st_L[h0]);
+  out[h1 * kHeadDim + d0] = f2bf(acc[1] / st_L[h1]);
   if (tid == 0) p.tickets[m * p.kv_heads + g] = 0u;
 }
 

@@ -171,6 +171,16 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
   return v;
 }
+// Ticket counter of a CTA group at GPU scope with acquire-release semantics:
+// called by one thread after a barrier of its CTA, it publishes every write
+// the CTA made before the barrier (release is cumulative over the barrier)
+// and orders the CTA's later reads, after another barrier, behind the writes
+// of the CTAs that took earlier tickets.
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 // Named barrier over `count` threads (multiple of 32) with id `id` (1..15).
 __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
