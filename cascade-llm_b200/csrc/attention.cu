@@ -106,11 +106,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
   // would otherwise stream weights during this kernel's latency-bound
   // publish/merge and slow it (decode step 3.37 -> 3.12 ms measured).
   grid_dep_wait();
-  float q[kGroup][4];
-  attn_load_q(p, m, g, q);
+  uint64_t qd[kGroup][4];
+  attn_load_q(p, m, g, qd);
   AttnWarpState ws;
   attn_state_init(ws);
-  float* pw = reinterpret_cast<float*>(scratch + AttnScratch::PW) + warp * 40;
+  float* pw = reinterpret_cast<float*>(scratch + AttnScratch::PW) + warp * 80;
   int stage = 0;
   uint32_t phase = 0;
   bool failed = false;  // a timed-out wait records the error; control flow is unchanged
@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
     const int64_t t0 = start + int64_t(i) * kSub;
     const int rows = int(min(int64_t(kSub), stop - t0));
     if (!failed && !mbar_wait(&full[stage], phase, p.err, 203)) failed = true;
-    attn_rows(ks + size_t(stage) * kSub * kHeadDim, vs + size_t(stage) * kSub * kHeadDim, rows, q, ws, pw);
+    attn_rows(ks + size_t(stage) * kSub * kHeadDim, vs + size_t(stage) * kSub * kHeadDim, rows, qd, ws, pw);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
     if (++stage == kAttnStages) {

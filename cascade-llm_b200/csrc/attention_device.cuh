@@ -34,11 +34,12 @@ constexpr int kRowsPerWarp = kSub / kAttnWarps;  // 8 rows of a sub-chunk per wa
 constexpr int kMergeBlock = 24;                    // splits merged per round trip
 
 // Shared-memory scratch of the compute part: per-warp broadcast areas (p of
-// the warp's 8 rows x 4 heads, alpha of 4 heads), per-warp softmax states and
-// the merge staging. The cross-warp combine of o reuses the K ring.
+// the warp's 8 rows x 4 heads and alpha of 4 heads, each value stored twice
+// as an f32x2 operand), per-warp softmax states and the merge staging. The
+// cross-warp combine of o reuses the K ring.
 struct AttnScratch {
-  static constexpr size_t PW = 0;                                     // [8 warps][40] fp32
-  static constexpr size_t WML = PW + kAttnWarps * 40 * 4;             // [8][4] m, [8][4] l
+  static constexpr size_t PW = 0;                                     // [8 warps][80] fp32
+  static constexpr size_t WML = PW + kAttnWarps * 80 * 4;             // [8][4] m, [8][4] l
   static constexpr size_t MRG = WML + 2 * kAttnWarps * kGroup * 4;    // merge: w [4][24]; M, L, s [4]; flag
   static constexpr size_t BYTES = MRG + (kGroup * kMergeBlock + 3 * kGroup + 4) * 4;
 };
@@ -57,17 +58,35 @@ __device__ __forceinline__ int attn_range(const AttnParams& p, int s, int m, int
   return start < stop ? int((stop - start + kSub - 1) / kSub) : 0;
 }
 
-// This lane's 4 dims of the 4 query heads of KV head g (token m).
-__device__ __forceinline__ void attn_load_q(const AttnParams& p, int m, int g, float (&q)[kGroup][4]) {
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): each component is rounded as
+// the scalar fma / mul would round it.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  return uint64_t(__float_as_uint(lo)) | (uint64_t(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ float f2lo(uint64_t v) { return __uint_as_float(uint32_t(v)); }
+__device__ __forceinline__ float f2hi(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// This lane's 4 dims of the 4 query heads of KV head g (token m), each value
+// twice (qd[h][i] = {q, q}) to multiply two K rows at once.
+__device__ __forceinline__ void attn_load_q(const AttnParams& p, int m, int g, uint64_t (&qd)[kGroup][4]) {
   const int lane = threadIdx.x & 31;
   const uint16_t* qrow = p.q + (int64_t(m) * p.kv_heads * kGroup + g * kGroup) * kHeadDim + 4 * lane;
 #pragma unroll
   for (int h = 0; h < kGroup; ++h) {
     const uint2 u = __ldcg(reinterpret_cast<const uint2*>(qrow + h * kHeadDim));
-    q[h][0] = bf16lo(u.x);
-    q[h][1] = bf16hi(u.x);
-    q[h][2] = bf16lo(u.y);
-    q[h][3] = bf16hi(u.y);
+    const float q4[4] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y)};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qd[h][i] = f2pack(q4[i], q4[i]);
   }
 }
 
@@ -75,15 +94,13 @@ __device__ __forceinline__ void attn_load_q(const AttnParams& p, int m, int g, f
 // the 8 lanes of a head hold the same values) and accumulates o[h][0..3] for
 // dims 4L..4L+3 of all 4 heads, unnormalised, relative to m_run.
 struct AttnWarpState {
-  float o[kGroup][4];
+  uint64_t o[kGroup][2];  // {dims 4L, 4L+1}, {4L+2, 4L+3} of each head
   float m_run, l_run;
 };
 
 __device__ __forceinline__ void attn_state_init(AttnWarpState& w) {
 #pragma unroll
-  for (int h = 0; h < kGroup; ++h)
-#pragma unroll
-    for (int d = 0; d < 4; ++d) w.o[h][d] = 0.f;
+  for (int h = 0; h < kGroup; ++h) w.o[h][0] = w.o[h][1] = 0ull;
   w.m_run = -__int_as_float(0x7F800000);
   w.l_run = 0.f;
 }
@@ -94,22 +111,29 @@ __device__ __forceinline__ void attn_state_init(AttnWarpState& w) {
 //           (32 partial sums); a transposed butterfly (16+8+4+2+1 shuffles)
 //           leaves lane L the full dot of row L >> 2, head L & 3;
 //   softmax running max / sum per head over the 8 lanes of the head;
-//   PV      p and the rescale factors go through the warp's 40-float area;
-//           each lane accumulates its 4 dims of the 4 heads.
+//   PV      p and the rescale factors go through the warp's 80-float area
+//           (each stored twice); each lane accumulates its 4 dims of the 4
+//           heads. Products and sums use f32x2 pairs (two K rows, or two
+//           dims) in the same order as the scalar code.
 __device__ __forceinline__ void attn_rows(const uint16_t* kst, const uint16_t* vst, int rows,
-                                          const float (&q)[kGroup][4], AttnWarpState& st, float* pw) {
+                                          const uint64_t (&qd)[kGroup][4], AttnWarpState& st, float* pw) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = warp * kRowsPerWarp;
   if (r0 >= rows) return;  // warp-uniform: no row of this warp in the sub-chunk
   float v[kRowsPerWarp * kGroup];
 #pragma unroll
-  for (int j = 0; j < kRowsPerWarp; ++j) {
-    uint2 u = make_uint2(0u, 0u);
+  for (int j = 0; j < kRowsPerWarp; j += 2) {  // rows j, j + 1 as the two halves of each pair
+    uint2 u = make_uint2(0u, 0u), w = make_uint2(0u, 0u);
     if (r0 + j < rows) u = *reinterpret_cast<const uint2*>(kst + (r0 + j) * kHeadDim + 4 * lane);
-    const float k0 = bf16lo(u.x), k1 = bf16hi(u.x), k2 = bf16lo(u.y), k3 = bf16hi(u.y);
+    if (r0 + j + 1 < rows) w = *reinterpret_cast<const uint2*>(kst + (r0 + j + 1) * kHeadDim + 4 * lane);
+    const uint64_t k0 = f2pack(bf16lo(u.x), bf16lo(w.x)), k1 = f2pack(bf16hi(u.x), bf16hi(w.x));
+    const uint64_t k2 = f2pack(bf16lo(u.y), bf16lo(w.y)), k3 = f2pack(bf16hi(u.y), bf16hi(w.y));
 #pragma unroll
-    for (int h = 0; h < kGroup; ++h)
-      v[j * kGroup + h] = fmaf(q[h][0], k0, fmaf(q[h][1], k1, fmaf(q[h][2], k2, q[h][3] * k3)));
+    for (int h = 0; h < kGroup; ++h) {
+      const uint64_t d = ffma2(qd[h][0], k0, ffma2(qd[h][1], k1, ffma2(qd[h][2], k2, fmul2(qd[h][3], k3))));
+      v[j * kGroup + h] = f2lo(d);
+      v[(j + 1) * kGroup + h] = f2hi(d);
+    }
   }
   // level `half`: the lane whose bit `half` is set keeps the upper half of
   // its values and receives the partner's copy of it, the other the lower
@@ -136,26 +160,33 @@ __device__ __forceinline__ void attn_rows(const uint16_t* kst, const uint16_t* v
   const float alpha = expf(st.m_run - m_new);  // 0 while m_run is -inf
   st.l_run = st.l_run * alpha + ps;
   st.m_run = m_new;
-  pw[lane] = p;  // [row j][head h] at 4j + h
-  if (lane < kGroup) pw[32 + lane] = alpha;
+  // [row j][head h] at 2 (4j + h), alpha of head h at 64 + 2h, each twice
+  *reinterpret_cast<float2*>(pw + 2 * lane) = make_float2(p, p);
+  if (lane < kGroup) *reinterpret_cast<float2*>(pw + 64 + 2 * lane) = make_float2(alpha, alpha);
   __syncwarp();
-  const float4 al = *reinterpret_cast<const float4*>(pw + 32);
-  const float a4[kGroup] = {al.x, al.y, al.z, al.w};
+  {
+    const ulonglong2 a01 = *reinterpret_cast<const ulonglong2*>(pw + 64);
+    const ulonglong2 a23 = *reinterpret_cast<const ulonglong2*>(pw + 68);
+    const uint64_t a4[kGroup] = {a01.x, a01.y, a23.x, a23.y};
 #pragma unroll
-  for (int h = 0; h < kGroup; ++h)
-#pragma unroll
-    for (int d = 0; d < 4; ++d) st.o[h][d] *= a4[h];
+    for (int h = 0; h < kGroup; ++h) {
+      st.o[h][0] = fmul2(st.o[h][0], a4[h]);
+      st.o[h][1] = fmul2(st.o[h][1], a4[h]);
+    }
+  }
 #pragma unroll
   for (int j = 0; j < kRowsPerWarp; ++j) {
     if (r0 + j < rows) {  // warp-uniform; rows past the end may hold stale bytes
-      const float4 pj = *reinterpret_cast<const float4*>(pw + 4 * j);
+      const ulonglong2 p01 = *reinterpret_cast<const ulonglong2*>(pw + 8 * j);
+      const ulonglong2 p23 = *reinterpret_cast<const ulonglong2*>(pw + 8 * j + 4);
       const uint2 u = *reinterpret_cast<const uint2*>(vst + (r0 + j) * kHeadDim + 4 * lane);
-      const float vv[4] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y)};
-      const float pp[kGroup] = {pj.x, pj.y, pj.z, pj.w};
+      const uint64_t v01 = f2pack(bf16lo(u.x), bf16hi(u.x)), v23 = f2pack(bf16lo(u.y), bf16hi(u.y));
+      const uint64_t pp[kGroup] = {p01.x, p01.y, p23.x, p23.y};
 #pragma unroll
-      for (int h = 0; h < kGroup; ++h)
-#pragma unroll
-        for (int d = 0; d < 4; ++d) st.o[h][d] = fmaf(pp[h], vv[d], st.o[h][d]);
+      for (int h = 0; h < kGroup; ++h) {
+        st.o[h][0] = ffma2(pp[h], v01, st.o[h][0]);
+        st.o[h][1] = ffma2(pp[h], v23, st.o[h][1]);
+      }
     }
   }
   __syncwarp();  // pw is rewritten by the next batch
@@ -187,7 +218,7 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, in
     const float mw = wm[warp * kGroup + h];
     const float f = mw == ninf ? 0.f : expf(mw - mm);
     *reinterpret_cast<float4*>(ring + (warp * kGroup + h) * kHeadDim + 4 * lane) =
-        make_float4(st.o[h][0] * f, st.o[h][1] * f, st.o[h][2] * f, st.o[h][3] * f);
+        make_float4(f2lo(st.o[h][0]) * f, f2hi(st.o[h][0]) * f, f2lo(st.o[h][1]) * f, f2hi(st.o[h][1]) * f);
   }
   sync();
   for (int e = tid; e < kGroup * kHeadDim; e += kAttnConsumers) {
