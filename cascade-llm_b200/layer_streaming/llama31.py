@@ -239,6 +239,8 @@ class Llama31DecodeExecutor:
                 ops.lm_head_workspace_bytes(self.top_k), dtype=torch.uint8, device=self.device
             )
             self.lm_ticket = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self._ids_dev = torch.zeros(1, dtype=torch.int64, device=self.device)  # one-token step input
+        self._embed_pending = False
         self.sm_count = int(lib.cb_sm_count())
         self._graphs = {}
         self._rows = 0
@@ -301,12 +303,20 @@ class Llama31DecodeExecutor:
             self.kv_cache.reserve(past + tokens)
             self._buffers(tokens)
             ids = input_ids.reshape(-1)
-            if ids.device != self.device or ids.dtype != torch.int64 or not ids.is_contiguous():
-                ids = ids.to(device=self.device, dtype=torch.int64).contiguous()
-            if self.vocab_runtime is None:
-                ops.embedding(ids, self.resident["model.embed_tokens.weight"], self._x[:tokens])
+            if tokens == 1 and self.vocab_runtime is None:
+                # one-token step: the id goes into a persistent device slot
+                # (asynchronous from pinned memory) and the embedding runs
+                # with the first unit, inside the step's graph when replayed
+                self._ids_dev.copy_(ids, non_blocking=True)
+                self._embed_pending = True
             else:
-                self._x[:tokens].copy_(self.vocab_runtime.embedding(ids.view(1, -1)).view(tokens, -1))
+                if ids.device != self.device or ids.dtype != torch.int64 or not ids.is_contiguous():
+                    ids = ids.to(device=self.device, dtype=torch.int64).contiguous()
+                self._embed_pending = False
+                if self.vocab_runtime is None:
+                    ops.embedding(ids, self.resident["model.embed_tokens.weight"], self._x[:tokens])
+                else:
+                    self._x[:tokens].copy_(self.vocab_runtime.embedding(ids.view(1, -1)).view(tokens, -1))
         self._tokens = tokens
         return DecodeState(
             hidden_states=self._x[:tokens].view(1, tokens, 4096),
@@ -389,7 +399,13 @@ class Llama31DecodeExecutor:
         ops.position_advance(self.kv_cache.position, self._tokens)
         self.kv_cache.length += self._tokens
 
+    def _embed_one(self):
+        ops.embedding(self._ids_dev, self.resident["model.embed_tokens.weight"], self._x[:1])
+
     def __call__(self, unit, weights, state):
+        if self._embed_pending:
+            self._embed_one()
+            self._embed_pending = False
         for operation in _UNIT_OPS.get(unit.operation, (unit.operation,)):
             self._unit(unit.layer_index, operation, weights)
         if unit.layer_index == self.config.num_hidden_layers - 1 and unit.operation in ("layer", "down_proj"):
@@ -408,13 +424,16 @@ class Llama31DecodeExecutor:
         bucket = max(64, 1 << (length - 1).bit_length())
         bucket = min(bucket, self.kv_cache.capacity)
         splits, chunk = self.attention_config(1, bucket)
-        key = (id(runtime), bucket, self.kv_cache.generation, self._rows)
+        embed = self._embed_pending  # the graph starts with the embedding of the step's id
+        key = (id(runtime), bucket, self.kv_cache.generation, self._rows, embed)
         graph = self._graphs.get(key)
         if graph is None:
             self._attention_workspace(1, splits)
             graph = torch.cuda.CUDAGraph()
             saved = self.kv_cache.length
             with torch.cuda.graph(graph):
+                if embed:
+                    self._embed_one()
                 for index, unit in enumerate(units):
                     for operation in _UNIT_OPS.get(unit.operation, (unit.operation,)):
                         self._unit(unit.layer_index, operation, runtime.unit_views(index), splits, chunk)
@@ -422,6 +441,7 @@ class Llama31DecodeExecutor:
             self.kv_cache.length = saved
             self._graphs[key] = graph
         graph.replay()
+        self._embed_pending = False
         self.kv_cache.length += 1
         return state
 
