@@ -247,15 +247,21 @@ def time_e2e(executor, runtime, token, steps):
     ids_host[0, 0] = int(token.reshape(-1)[0])
     h2d = ids_host.numel() * ids_host.element_size()
     d2h = 0
+    values_host = indices_host = None
     with torch.inference_mode():
         torch.cuda.synchronize()
         started = time.perf_counter()
         for _ in range(steps):
             state = step(executor, runtime, ids_host)
-            values = state.topk_values.cpu()
-            indices = state.topk_indices.cpu()
-            d2h = values.numel() * values.element_size() + indices.numel() * indices.element_size()
-            ids_host[0, 0] = int(indices.reshape(-1)[0])
+            if values_host is None:
+                values_host = torch.empty(state.topk_values.shape, dtype=state.topk_values.dtype).pin_memory()
+                indices_host = torch.empty(state.topk_indices.shape, dtype=state.topk_indices.dtype).pin_memory()
+            # both results copied asynchronously, one wait for the step
+            values_host.copy_(state.topk_values, non_blocking=True)
+            indices_host.copy_(state.topk_indices, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            d2h = values_host.numel() * values_host.element_size() + indices_host.numel() * indices_host.element_size()
+            ids_host[0, 0] = int(indices_host.reshape(-1)[0])
         elapsed = time.perf_counter() - started
     return {"value": elapsed * 1000.0 / steps, "unit": "ms/token", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h}
@@ -713,10 +719,15 @@ def tensor_parallel(args, world, rank, local, device):
         torch.cuda.synchronize()
         barrier()
         started = time.perf_counter()
+        values = indices = None
         for _ in range(args.steps):
             state = decoder(ids_host)
-            values = state.topk_values.cpu()
-            indices = state.topk_indices.cpu()
+            if values is None:
+                values = torch.empty(state.topk_values.shape, dtype=state.topk_values.dtype).pin_memory()
+                indices = torch.empty(state.topk_indices.shape, dtype=state.topk_indices.dtype).pin_memory()
+            values.copy_(state.topk_values, non_blocking=True)  # both results, one wait per step
+            indices.copy_(state.topk_indices, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
             ids_host[0, 0] = int(indices.reshape(-1)[0])
         e2e_ms = (time.perf_counter() - started) * 1000.0 / args.steps
     t = torch.tensor([e2e_ms], device=device)

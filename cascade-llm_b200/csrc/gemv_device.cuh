@@ -569,13 +569,13 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   }
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
-    const unsigned int ticket = atomicAdd(p.ticket, 1u);
+    // acq_rel: publishes this CTA's candidates (written before the barrier)
+    // and, for the last CTA, orders its reads after everyone's
+    const unsigned int ticket = atom_add_acq_rel_gpu(p.ticket, 1u);
     red[15] = __int_as_float(ticket == unsigned(ncta - 1) ? 1 : 0);
   }
   __syncthreads();
   if (__float_as_int(red[15]) != 1) return;
-  __threadfence();
   block_merge_topk(p.cand_values, p.cand_indices, ncta, p.k, p.out_values, p.out_indices, red, lrow);
   if (tid == 0) *p.ticket = 0u;
   if (!p.world) return;
