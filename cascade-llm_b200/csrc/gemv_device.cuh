@@ -471,6 +471,19 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   const int kp = S::kpart(warp), ul = S::ulane(warp);  // K-part and unit lane of this warp
   const int kbase = kp * S::KS + lane * 8;
 
+  // this warp's activation slice: registers, or (XSMEM) its own region of
+  // shared memory, written and read by the same warp only. In register form
+  // the slice (and its RMSNorm weights) is loaded before the norm's
+  // reduction, so both loads share one round trip.
+  uint4 xr[S::XSMEM ? 1 : S::CPL];
+  uint4 nw[S::XSMEM ? 1 : S::CPL];
+  if constexpr (!S::XSMEM) {
+#pragma unroll
+    for (int c = 0; c < S::CPL; ++c) {
+      xr[c] = ld_cg_u4(p.x + kbase + c * 256);
+      if (p.norm_w) nw[c] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + kbase + c * 256));
+    }
+  }
   float inv = 1.0f;
   if (p.norm_w) {
     float ss = 0.f;
@@ -491,20 +504,19 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
     for (int q = 0; q < S::WARPS; ++q) tot += red[q];
     inv = rsqrtf(tot * (1.0f / K) + p.eps);
   }
-  // this warp's activation slice: registers, or (XSMEM) its own region of
-  // shared memory, written and read by the same warp only
-  uint4 xr[S::XSMEM ? 1 : S::CPL];
   uint4* xw = reinterpret_cast<uint4*>(smem + S::XS) + warp * (S::KS / 8) + lane;  // this warp's region
+  if constexpr (S::XSMEM) {
 #pragma unroll
-  for (int c = 0; c < S::CPL; ++c) {
-    uint4 v = ld_cg_u4(p.x + kbase + c * 256);
-    if (p.norm_w) v = normalize8(v, __ldg(reinterpret_cast<const uint4*>(p.norm_w + kbase + c * 256)), inv);
-    if constexpr (S::XSMEM)
+    for (int c = 0; c < S::CPL; ++c) {
+      uint4 v = ld_cg_u4(p.x + kbase + c * 256);
+      if (p.norm_w) v = normalize8(v, __ldg(reinterpret_cast<const uint4*>(p.norm_w + kbase + c * 256)), inv);
       xw[c * 32] = v;
-    else
-      xr[c] = v;
+    }
+    __syncwarp();
+  } else if (p.norm_w) {
+#pragma unroll
+    for (int c = 0; c < S::CPL; ++c) xr[c] = normalize8(xr[c], nw[c], inv);
   }
-  if constexpr (S::XSMEM) __syncwarp();
 
   // dot products of one batch held in registers
   auto consume = [&](const GemvRegs<K, DEPTH>& rr, int ub) {
