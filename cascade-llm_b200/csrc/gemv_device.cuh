@@ -284,8 +284,10 @@ __device__ __forceinline__ uint4 ld_stream(const uint16_t* p) {
   return r;
 }
 
+// pre: aux_a / aux_b (the bf16 residual or gate values of rows A / B) and
+// freq (the RoPE inverse frequency) were loaded earlier by this thread.
 static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int j, float a, float b,
-                              int pos) {
+                              int pos, bool pre, float aux_a, float aux_b, float freq) {
   int64_t oa = int64_t(j / sg.group) * sg.head_stride + (j % sg.group);
   if (sg.pos_stride) {
     if (pos < 0 || pos >= sg.pos_limit) {  // never write outside the cache
@@ -301,14 +303,14 @@ static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int
       sg.out[ob] = f2bf(b);
       break;
     case EPI_RESIDUAL:
-      sg.out[oa] = f2bf(bf16f(__ldcg(sg.aux + oa)) + rbf(a));
-      sg.out[ob] = f2bf(bf16f(__ldcg(sg.aux + ob)) + rbf(b));
+      sg.out[oa] = f2bf((pre ? aux_a : bf16f(__ldcg(sg.aux + oa))) + rbf(a));
+      sg.out[ob] = f2bf((pre ? aux_b : bf16f(__ldcg(sg.aux + ob))) + rbf(b));
       break;
     case EPI_ROPE: {
       // transformers modeling_llama.py:124-168: cos/sin of (inv_freq * pos)
       // in fp32, cast to bf16; q*cos + rotate_half(q)*sin in bf16.
       uint16_t ra, rb;
-      rope_pair(a, b, __ldg(p.inv_freq + j % sg.group), pos, ra, rb);
+      rope_pair(a, b, pre ? freq : __ldg(p.inv_freq + j % sg.group), pos, ra, rb);
       sg.out[oa] = ra;
       sg.out[ob] = rb;
       break;
@@ -318,8 +320,8 @@ static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int
       sg.out[ob] = f2bf(silu_bf16(rbf(b)));
       break;
     case EPI_MUL:
-      sg.out[oa] = f2bf(bf16f(__ldcg(sg.aux + oa)) * rbf(a));
-      sg.out[ob] = f2bf(bf16f(__ldcg(sg.aux + ob)) * rbf(b));
+      sg.out[oa] = f2bf((pre ? aux_a : bf16f(__ldcg(sg.aux + oa))) * rbf(a));
+      sg.out[ob] = f2bf((pre ? aux_b : bf16f(__ldcg(sg.aux + ob))) * rbf(b));
       break;
     case EPI_SWIGLU:
       sg.out[oa] = f2bf(silu_bf16(rbf(a)) * rbf(b));
@@ -354,8 +356,8 @@ static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int
         }
       }
       if (late && p.err) atomicExch(p.err, 120);
-      sg.out[oa] = f2bf(bf16f(__ldcg(sg.aux + oa)) + rbf(sa));
-      sg.out[ob] = f2bf(bf16f(__ldcg(sg.aux + ob)) + rbf(sb));
+      sg.out[oa] = f2bf((pre ? aux_a : bf16f(__ldcg(sg.aux + oa))) + rbf(sa));
+      sg.out[ob] = f2bf((pre ? aux_b : bf16f(__ldcg(sg.aux + ob))) + rbf(sb));
       break;
     }
     default:
@@ -504,6 +506,26 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
     for (int q = 0; q < S::WARPS; ++q) tot += red[q];
     inv = rsqrtf(tot * (1.0f / K) + p.eps);
   }
+  // The epilogue operands of this thread's first unit (and the position) are
+  // loaded here, in the same round trip as the activations, so the epilogue
+  // after the main loop needs no further load.
+  const int pos = p.pos ? __ldcg(p.pos) + p.token : 0;
+  bool pre = false;
+  float pre_a = 0.f, pre_b = 0.f, pre_f = 0.f;
+  if (tid < units) {
+    int seg, j;
+    gemv_locate(p, u0 + tid, seg, j);
+    const Segment& sg = p.seg[seg];
+    if (sg.mode == EPI_RESIDUAL || sg.mode == EPI_MUL || sg.mode == EPI_EXCHANGE) {
+      const int64_t oa = int64_t(j / sg.group) * sg.head_stride + (j % sg.group);  // no position stride
+      pre_a = bf16f(__ldcg(sg.aux + oa));
+      pre_b = bf16f(__ldcg(sg.aux + oa + sg.b_offset));
+      pre = true;
+    } else if (sg.mode == EPI_ROPE) {
+      pre_f = __ldg(p.inv_freq + j % sg.group);
+      pre = true;
+    }
+  }
   uint4* xw = reinterpret_cast<uint4*>(smem + S::XS) + warp * (S::KS / 8) + lane;  // this warp's region
   if constexpr (S::XSMEM) {
 #pragma unroll
@@ -546,7 +568,6 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   }
   __syncthreads();
 
-  const int pos = p.pos ? __ldcg(p.pos) + p.token : 0;
   for (int i = tid; i < units; i += kThreads) {
     float a = 0.f, b = 0.f;
 #pragma unroll
@@ -567,7 +588,7 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
       lrow[i] = la;
       lrow[units + i] = lb;
     } else {
-      gemv_epilogue(p, sg, j, a, b, pos);
+      gemv_epilogue(p, sg, j, a, b, pos, pre && i == tid, pre_a, pre_b, pre_f);
     }
   }
 
