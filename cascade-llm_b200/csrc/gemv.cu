@@ -12,22 +12,23 @@
 //            last-CTA merge into the launch's exact top-k
 //
 // Design (HBM-bound: 0.5 FMA per weight byte):
-//   * one CTA per SM (grid = SM count), 8 consumer warps + 1 producer warp;
+//   * two CTAs of 8 warps per SM (grid = 2 x SM count), <= 128 registers;
 //   * work is a list of "units"; a unit is a PAIR of weight rows (A, B) whose
 //     outputs an epilogue needs together: rows d and d+64 of one head for
 //     RoPE, gate row j and up row j for SwiGLU, rows j and j+N/2 otherwise.
-//     Units are split evenly over CTAs (row granularity, <=1.2% imbalance);
-//   * the producer streams tiles of T units (2T contiguous-row slabs) with
-//     cp.async.bulk into an NSTAGE-deep shared-memory ring, tracked by
-//     mbarriers, with an L2 evict_first hint (weights are read once);
-//   * the producer starts streaming BEFORE griddepcontrol.wait (weights do
-//     not depend on the previous kernel), so with programmatic dependent
-//     launch the next projection's weights are already in flight while the
-//     previous kernel drains;
-//   * consumers hold their slice of the activation vector in registers for
-//     the whole kernel; each warp owns one row of a tile and 1/WPR of K, so
-//     smem reads are 512 contiguous bytes per warp instruction (no bank
-//     conflicts) and the reduction is one warp shuffle tree + WPR partials.
+//     Each CTA owns a contiguous range of units (row granularity);
+//   * CTA-cooperative split-K: every warp streams its 1/8 of K for every unit
+//     of the range straight into registers (128-bit ld.global.nc, a batch of
+//     up to 16 loads in flight per lane), reduces with shuffles into shared
+//     memory, and after ONE barrier the epilogues of all units run in
+//     parallel, one thread per unit;
+//   * the first batch of weight loads is issued BEFORE griddepcontrol.wait
+//     (weights do not depend on the previous kernel), so with programmatic
+//     dependent launch the next projection's weights are in flight while the
+//     previous kernel drains; everything read from the previous kernel (the
+//     activation slice, RMSNorm weights, the epilogue's residual / gate
+//     values, RoPE frequency and position) is requested in one round trip
+//     right after the wait.
 #include <cuda_bf16.h>
 
 #include <algorithm>

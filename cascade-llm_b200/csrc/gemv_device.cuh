@@ -1,6 +1,5 @@
 // Device-side building blocks of the weight-streaming GEMV (BF16 weights,
-// fp32 accumulate), shared by the stand-alone projection kernels (gemv.cu)
-// and the persistent decode-step kernel (decode_step.cu).
+// fp32 accumulate) of the projection kernels (gemv.cu).
 #pragma once
 
 #include "common.cuh"
@@ -639,7 +638,7 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   if (warp == 0) warp_select_rows_idx(sv, si, p.world * k, k, p.out_values, p.out_indices);
 }
 
-// Host-side parameter builders (gemv.cu), shared with the decode-step table.
+// Host-side parameter builders (gemv.cu).
 int finish_params(GemvParams& p);
 int build_qkv_params(GemvParams& p, const void* x, const void* norm_w, float eps, const void* wq,
                      const void* wk, const void* wv, const float* inv_freq, const int32_t* position,

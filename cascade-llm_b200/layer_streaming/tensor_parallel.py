@@ -320,6 +320,7 @@ class TensorParallelDecoder:
             self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
             self.values = torch.empty((1, 1, self.top_k), dtype=torch.float32, device=self.device)
             self.indices = torch.empty((1, 1, self.top_k), dtype=torch.int64, device=self.device)
+            self._ids_dev = torch.zeros(1, dtype=torch.int64, device=self.device)  # one-token step input
         self.exchange_buffers = ExchangeBuffers(self.group, self.device) if exchange == "peer" else None
         self.sm_count = int(lib.cb_sm_count())
         self._graphs = {}
@@ -473,11 +474,14 @@ class TensorParallelDecoder:
         with torch.cuda.device(self.device):
             self.kv_cache.reserve(past + tokens)
             self._buffers(tokens)
-            ids = input_ids.reshape(-1).to(device=self.device, dtype=torch.int64)
-            ops.embedding(ids, self.weights["model.embed_tokens.weight"], self._x[:tokens])
             if tokens == 1 and self.use_graphs:
+                # the id goes into a persistent device slot (asynchronous from
+                # pinned memory); the step's graph starts with its embedding
+                self._ids_dev.copy_(input_ids.reshape(-1), non_blocking=True)
                 self._replay()
             else:
+                ids = input_ids.reshape(-1).to(device=self.device, dtype=torch.int64)
+                ops.embedding(ids, self.weights["model.embed_tokens.weight"], self._x[:tokens])
                 splits, chunk = self.attention_config(tokens, past + tokens)
                 self._step(tokens, splits, chunk)
         self.kv_cache.length += tokens
@@ -499,6 +503,7 @@ class TensorParallelDecoder:
             self._attention_workspace(1, splits)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
+                ops.embedding(self._ids_dev, self.weights["model.embed_tokens.weight"], self._x[:1])
                 self._step(1, splits, chunk)
             # every rank captured the same graph; start replaying together
             torch.cuda.synchronize(self.device)
