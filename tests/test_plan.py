@@ -95,3 +95,24 @@ def test_unknown_tensor_raises():
         build_llama31_8b_plan().tensor_host_offset("model.layers.99.bogus")
     with pytest.raises(ValueError):
         build_llama31_8b_plan(stream_vocab=True, vocab_chunk_bytes=100)
+
+
+@pytest.mark.parametrize("kv_heads", [8, 4, 2, 1])
+def test_attention_split_policy(kv_heads):
+    """The split-KV layout covers every position with chunks of whole 64-position
+    sub-chunks and targets about two CTAs per SM (148 SMs), within the kernel's
+    grid limits and the allocation-free entry point's one-token capacity."""
+
+    from layer_streaming.llama31 import attention_split
+
+    sms = 148
+    for tokens in (1, 2, 6):
+        for length in (1, 63, 64, 65, 2048, 2049, 4096, 8192, 32768, 131072):
+            splits, chunk = attention_split(tokens, length, sms, kv_heads=kv_heads)
+            assert chunk >= 64 and chunk % 64 == 0
+            assert splits * chunk >= length and (splits - 1) * chunk < length  # no empty split
+            assert 1 <= splits <= 65535
+            ctas = splits * kv_heads * tokens
+            assert ctas <= max(2 * sms, kv_heads * tokens) or chunk == 64
+            if tokens == 1 and kv_heads == 8:
+                assert splits <= 252  # cb_attention_noalloc holds 252 one-token splits
