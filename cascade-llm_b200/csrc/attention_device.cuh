@@ -53,6 +53,8 @@ __device__ __forceinline__ int attn_range(const AttnParams& p, int s, int m, int
     if (threadIdx.x == 0 && p.err) atomicExch(p.err, 201);
     visible = p.cache_len;
   }
+  if (visible > int64_t(p.splits) * p.chunk && s == 0 && threadIdx.x == 0 && p.err)
+    atomicExch(p.err, 204);  // too few splits for this position: the tail is left out
   start = int64_t(s) * p.chunk;
   stop = min(start + int64_t(p.chunk), visible);
   return start < stop ? int((stop - start + kSub - 1) / kSub) : 0;

@@ -140,11 +140,13 @@ __device__ __forceinline__ uint64_t ld_tagged(const uint64_t* p) {
 }
 // Wait until the word at p carries `tag`, for at most `limit_ns` of wall
 // clock and kSpinLimit x 16 polls, whichever ends first; returns the payload
-// and sets *timed_out on time-out (the payload is then undefined).
+// and sets *timed_out on time-out (the payload is then undefined). Once
+// *timed_out is set, later calls of the same thread only look once, so a
+// missing peer costs one limit per thread, not one per awaited word.
 __device__ __forceinline__ uint32_t wait_tagged(const uint64_t* p, uint32_t tag, uint64_t limit_ns,
                                                 bool* timed_out) {
   uint64_t w = ld_tagged(p);
-  if (uint32_t(w >> 32) == tag) return uint32_t(w);
+  if (uint32_t(w >> 32) == tag || *timed_out) return uint32_t(w);
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < (kSpinLimit << 4); ++i) {
     w = ld_tagged(p);

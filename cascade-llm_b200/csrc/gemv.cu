@@ -331,6 +331,7 @@ static int set_exchange(GemvParams& p, const char* what, void* const* exchange, 
   p.slot = slot;
   p.slots = slots;
   p.epoch = epoch;
+  p.wait_ns = exchange_wait_ns();
   return kOk;
 }
 

@@ -36,7 +36,7 @@ constexpr size_t kXchgData = 0;
 constexpr size_t kXchgCandV = kXchgData + size_t(2) * kXchgMaxWorld * kXchgWidth * 8;
 constexpr size_t kXchgCandI = kXchgCandV + size_t(2) * kXchgMaxWorld * 64 * 8;
 constexpr size_t kXchgBytes = kXchgCandI + size_t(2) * kXchgMaxWorld * 64 * 8;
-constexpr uint64_t kXchgWaitNs = 2000000000ull;  // a peer that is 2 s late is reported, not awaited
+constexpr uint64_t kXchgWaitNs = 2000000000ull;  // default limit: a peer 2 s late is reported, not awaited
 
 __device__ __forceinline__ uint64_t* xchg_data(uint8_t* base, int par, int rank) {
   return reinterpret_cast<uint64_t*>(base + kXchgData) + (par * kXchgMaxWorld + rank) * kXchgWidth;
@@ -94,6 +94,7 @@ struct GemvParams {
   int rank, world;
   int slot, slots;
   const int32_t* epoch;    // device step counter, advanced once per step
+  uint64_t wait_ns;        // how long a peer's word is awaited before the launch gives up
 };
 
 __device__ __forceinline__ int64_t unit_row(const Segment& s, int j) {
@@ -350,8 +351,8 @@ static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int
       for (int q = 0; q < kXchgMaxWorld; ++q) {
         if (q < p.world) {
           const uint64_t* d = xchg_data(p.xchg[p.rank], par, q);
-          sa += __uint_as_float(wait_tagged(d + oa, seq, kXchgWaitNs, &late));
-          sb += __uint_as_float(wait_tagged(d + ob, seq, kXchgWaitNs, &late));
+          sa += __uint_as_float(wait_tagged(d + oa, seq, p.wait_ns, &late));
+          sb += __uint_as_float(wait_tagged(d + ob, seq, p.wait_ns, &late));
         }
       }
       if (late && p.err) atomicExch(p.err, 120);
@@ -630,8 +631,8 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   bool late = false;
   uint8_t* own = p.xchg[p.rank];
   for (int e = tid; e < p.world * k; e += kThreads) {
-    sv[e] = __uint_as_float(wait_tagged(xchg_cand_v(own, par) + e, seq, kXchgWaitNs, &late));
-    si[e] = int64_t(wait_tagged(xchg_cand_i(own, par) + e, seq, kXchgWaitNs, &late));
+    sv[e] = __uint_as_float(wait_tagged(xchg_cand_v(own, par) + e, seq, p.wait_ns, &late));
+    si[e] = int64_t(wait_tagged(xchg_cand_i(own, par) + e, seq, p.wait_ns, &late));
   }
   if (late && p.err) atomicExch(p.err, 121);
   __syncthreads();

@@ -23,6 +23,8 @@ void set_error(const std::string& msg);
 int fail(int code, const char* fmt, ...);
 int check_launch(const char* what);
 bool pdl_enabled();
+// Wall-clock limit of the tensor-parallel exchange waits (cb_set_exchange_wait_ns).
+uint64_t exchange_wait_ns();
 int sm_count();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

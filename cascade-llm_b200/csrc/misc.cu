@@ -2,6 +2,7 @@
 // programmatic-dependent-launch switch, seeded initialisation, embedding
 // gather, stand-alone RMSNorm, top-k merge, the device position counter and
 // the H2D copy used by the streamed runtime.
+#include <atomic>
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
@@ -17,6 +18,7 @@ namespace cb {
 
 static thread_local std::string g_last_error;
 static bool g_pdl = true;
+static std::atomic<uint64_t> g_exchange_wait_ns{2000000000ull};
 static int32_t* g_error_word = nullptr;
 
 void set_error(const std::string& msg) { g_last_error = msg; }
@@ -38,6 +40,7 @@ int check_launch(const char* what) {
 }
 
 bool pdl_enabled() { return g_pdl; }
+uint64_t exchange_wait_ns() { return g_exchange_wait_ns.load(); }
 
 int sm_count() {
   int dev = 0, n = 0;
@@ -215,6 +218,9 @@ extern "C" int cb_set_pdl(int enable) {
   const int prev = g_pdl ? 1 : 0;
   g_pdl = enable != 0;
   return prev;
+}
+extern "C" uint64_t cb_set_exchange_wait_ns(uint64_t ns) {
+  return g_exchange_wait_ns.exchange(ns ? ns : 2000000000ull);
 }
 extern "C" int cb_sm_count(void) { return sm_count(); }
 extern "C" int cb_prepare(void) {

@@ -67,6 +67,7 @@ _SIGNATURES = {
     "cb_ipc_handle": (_I, [_P, _P]),
     "cb_ipc_open": (_I, [_P, _PP]),
     "cb_ipc_close": (_I, [_P]),
+    "cb_set_exchange_wait_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "cb_proj_allreduce_residual": (_I, [_P, _I, _P, _I, _P, _P, _PP, _I, _I, _I, _I, _P, _P]),
     "cb_lm_head_topk_allgather": (
         _I, [_P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P, _P, _PP, _I, _I, _I, _I, _P, _P]

@@ -150,7 +150,9 @@ int cb_topk_merge(const float* a_values, const int64_t* a_indices, int na, const
  * q: [M, 4*kv_heads, 128]; k_cache/v_cache: this layer's [kv_heads, cache_len, 128];
  * kv_heads = 8, or a tensor-parallel rank's 8/N.
  * chunk = positions per split (multiple of 64); splits*chunk must cover the
- * longest context of the step. workspace: cb_attention_workspace_bytes(M,
+ * longest context of the step (the position lives on the device, so a launch
+ * whose splits fall short records code 204 in the error word; the positions
+ * beyond splits*chunk are then left out). workspace: cb_attention_workspace_bytes(M,
  * splits) bytes of scratch for the per-split partials (no initialisation).
  * tickets: M*kv_heads uint32 counters, zeroed once by the caller; each launch
  * leaves them zero. */
@@ -172,7 +174,12 @@ int cb_attention(const void* q, const void* k_cache, const void* v_cache, int64_
  * call before any stream capture. Each call clears its ticket range with a
  * cudaMemsetAsync and calls no cudaMalloc/cudaFree. All calls share the
  * scratch, so calls that overlap on the GPU (different streams) race.
- * Arguments otherwise as cb_attention. */
+ * Arguments otherwise as cb_attention, for the full 8-KV-head layout only
+ * (kv_heads = 8: the scratch and tickets are sized for it; a
+ * tensor-parallel rank's 1, 2 or 4 KV heads need cb_attention). The array's
+ * address is looked up once per device and kept for the life of the
+ * process: it assumes the device's primary context is never reset
+ * (cudaDeviceReset) while the library is loaded. */
 int cb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
                          const int32_t* position, int M, int splits, int chunk, void* out,
                          void* stream);
@@ -236,8 +243,9 @@ int cb_prefill_attention(const void* q, const void* k_cache, const void* v_cache
  * slots even, the same on every rank); `epoch` is a device int32 step counter
  * that every rank advances by one after each step (cb_position_advance).
  * Ranks must issue the same launches in the same order. A peer that does not
- * arrive within 2 s sets the error word (120: projection, 121: LM head) and
- * the launch completes with undefined values instead of hanging. */
+ * arrive within the exchange wait limit (default 2 s) sets the error word
+ * (120: projection, 121: LM head) and the launch completes with undefined
+ * values instead of hanging. */
 #define CB_IPC_HANDLE_BYTES 64
 int64_t cb_exchange_bytes(void);
 int cb_exchange_alloc(void** buffer_out);
@@ -245,6 +253,11 @@ int cb_exchange_free(void* buffer);
 int cb_ipc_handle(const void* buffer, void* handle_out);
 int cb_ipc_open(const void* handle, void** buffer_out);
 int cb_ipc_close(void* buffer);
+/* Sets the wall-clock limit of the exchange waits for launches issued from
+ * now on (a captured CUDA graph keeps the limit it was captured with); 0
+ * restores the 2 s default. Returns the previous limit. A short limit lets a
+ * test make a wait run out on one GPU. */
+uint64_t cb_set_exchange_wait_ns(uint64_t ns);
 
 /* Row-parallel projection fused with its all-reduce and the residual add:
  * out = bf16(residual + bf16(sum over ranks q of x_q . W_q^T)), where x_q / W_q

@@ -1,0 +1,156 @@
+"""Parity of the benchmarked path: chunked prefill + greedy decode (GPU).
+
+``bench.py`` fills a 2048-token KV cache with four 512-token prefill chunks
+and then times one-token decode steps; config 4 does the same at 32K. The
+reference refuses multi-token steps after its prefill
+(``layer_streaming/llama31.py:133-136, 221-222``), so its path here is the
+oracle's SINGLE-SHOT prefill of the same ids (the reference's torch ops over
+the same device weights), teacher-forced with the engine's greedy ids on the
+decode steps that follow.
+
+Criteria per step (the north-star ones, tolerance = 2e-2 + 2e-2 * |value|):
+  * the engine's top-k values within the tolerance of the oracle's;
+  * the engine's top-k ids equal to the oracle's at every rank whose gaps to
+    both neighbours exceed the tolerance;
+  * the engine's greedy id equal to the oracle's wherever the oracle's
+    top-1/top-2 gap exceeds the tolerance.
+Every step's ids, values and gaps are printed (``pytest -s``) as the record.
+"""
+
+import pytest
+import torch
+
+import parity
+from conftest import Config, engine_weights
+from oracle import llama_oracle as lo
+
+pytestmark = pytest.mark.gpu
+
+TOP_K = 10
+
+
+def random_ids(count, seed=1):
+    """The bench's prompt: uniform ids from a seeded CPU generator."""
+
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randint(0, 128256, (1, count), generator=gen)
+
+
+def engine_run(hbm_engine, ids, chunk, decode_steps, capacity):
+    """Chunked prefill of `ids` then `decode_steps` greedy steps through the
+    public API (begin -> runtime.run -> finish); per-step (values, ids) of
+    the last prefill chunk and of every decode step, and the executor."""
+
+    import layer_streaming as ls
+
+    _, _, resident, runtime = hbm_engine
+    executor = ls.Llama31DecodeExecutor(
+        Config(), resident, top_k=TOP_K, max_length=capacity, allow_chunked_prefill=True
+    )
+    out = []
+    with torch.inference_mode():
+        for begin in range(0, ids.shape[1], chunk):
+            state = executor.finish(runtime.run(executor, executor.begin(ids[:, begin:begin + chunk])))
+        out.append((state.topk_values.reshape(-1).cpu(), state.topk_indices.reshape(-1).cpu()))
+        token = state.topk_indices[..., 0]
+        for _ in range(decode_steps):
+            state = executor.finish(runtime.run(executor, executor.begin(token)))
+            out.append((state.topk_values.reshape(-1).cpu(), state.topk_indices.reshape(-1).cpu()))
+            token = state.topk_indices[..., 0]
+    executor.check_errors()
+    return out, executor
+
+
+def oracle_follow(oracle, first_ids, engine_steps):
+    """The oracle's steps fed `first_ids` and then the engine's greedy ids."""
+
+    out = []
+    with torch.inference_mode():
+        result = oracle.step(first_ids)
+        out.append((result["values"].reshape(-1).float().cpu(), result["indices"].reshape(-1).cpu()))
+        for values, indices in engine_steps[:-1]:
+            token = indices[:1].view(1, 1).to(first_ids.device)
+            result = oracle.step(token)
+            out.append((result["values"].reshape(-1).float().cpu(), result["indices"].reshape(-1).cpu()))
+    return out
+
+
+def compare(engine_steps, oracle_steps, label):
+    """Assert the per-step criteria; print the record."""
+
+    worst = 0.0
+    for step, ((ev, ei), (ov, oi)) in enumerate(zip(engine_steps, oracle_steps)):
+        tol = parity.ATOL + parity.RTOL * ov.abs()
+        diff = (ev - ov).abs()
+        worst = max(worst, float((diff / tol).max()))
+        gap = float(ov[0] - ov[1])
+        print("{} step {}: engine id {} oracle id {} | top-1/top-2 gap oracle {:.4f} engine {:.4f} "
+              "(tolerance {:.4f}) | max |dvalue| {:.4f}".format(
+                  label, step, int(ei[0]), int(oi[0]), gap, float(ev[0] - ev[1]), float(tol[0]),
+                  float(diff.max())))
+        assert bool((diff <= tol).all()), "{} step {}: values {} vs oracle {}".format(
+            label, step, ev.tolist(), ov.tolist())
+        for j in range(len(ov)):
+            before = float(ov[j - 1] - ov[j]) if j else float("inf")
+            after = float(ov[j] - ov[j + 1]) if j + 1 < len(ov) else 0.0
+            if before > float(tol[j]) and after > float(tol[j]):
+                assert int(ei[j]) == int(oi[j]), "{} step {} rank {}: id {} vs oracle {}".format(
+                    label, step, j, int(ei[j]), int(oi[j]))
+        if gap > float(tol[0]):
+            assert int(ei[0]) == int(oi[0]), "{} step {}: greedy id {} vs oracle {}".format(
+                label, step, int(ei[0]), int(oi[0]))
+    print("{}: worst |dvalue| / tolerance = {:.3f}".format(label, worst))
+    print("{}: engine greedy ids {}".format(label, [int(i[0]) for _, i in engine_steps]))
+
+
+@pytest.mark.parametrize("context,chunk,decode_steps", [(2048, 512, 8), (4096, 512, 4)])
+def test_chunked_prefill_then_decode_matches_single_shot(cuda, hbm_engine, context, chunk, decode_steps):
+    """2048 ids in 4 x 512 chunks + 8 decode steps (exactly what bench.py
+    times), and 4096 ids in 8 chunks, against the single-shot prefill."""
+
+    ids = random_ids(context).to(cuda)
+    engine_steps, executor = engine_run(hbm_engine, ids, chunk, decode_steps, context + decode_steps + 64)
+    assert executor.kv_cache.length == context + decode_steps
+    oracle = lo.OracleDecoder(engine_weights(hbm_engine), top_k=TOP_K)
+    oracle_steps = oracle_follow(oracle, ids, engine_steps)
+    compare(engine_steps, oracle_steps, "{}x{}".format(context // chunk, chunk))
+
+    # the engine's KV cache holds what the single-shot prefill computed
+    # (keys after RoPE), up to bf16 rounding of the projections
+    for layer in (0, 31):
+        ok, ov = oracle.cache[layer]
+        ek = executor.kv_cache.key(layer)[:, :context].float()
+        ev = executor.kv_cache.value(layer)[:, :context].float()
+        for name, got, ref in (("key", ek, ok[0, :, :context].float()), ("value", ev, ov[0, :, :context].float())):
+            err = (got - ref).abs()
+            bound = 2e-2 + 2e-2 * ref.abs()
+            frac = float((err > bound).float().mean())
+            print("layer {} cache {}: max |d| {:.4f}, fraction beyond tolerance {:.2e}".format(
+                layer, name, float(err.max()), frac))
+            if layer == 0:  # the first layer's inputs are identical: one-ulp agreement
+                assert frac == 0.0
+
+
+def test_decode_at_32k_context_matches_oracle_on_engine_cache(cuda, hbm_engine):
+    """Config 4: 32768 ids prefilled in 64 chunks of 512, then decode steps.
+    A CPU/torch prefill of 32K is the reference's own path only in principle
+    (it refuses chunks and its quadratic mask is 4 GiB per head group), so the
+    oracle is handed the engine's KV cache and runs the decode steps with the
+    reference's ops over it: attention over 32K positions, the projections
+    and the head, compared at every step."""
+
+    context = 32768
+    ids = random_ids(context).to(cuda)
+    engine_steps, executor = engine_run(hbm_engine, ids, 512, 3, context + 64)
+    oracle = lo.OracleDecoder(engine_weights(hbm_engine), top_k=TOP_K)
+    cache = executor.kv_cache
+    # the cache as it was after the prefill (the decode steps appended 3 rows)
+    oracle.cache = [
+        (cache.key(i)[:, :context].unsqueeze(0).clone(), cache.value(i)[:, :context].unsqueeze(0).clone())
+        for i in range(32)
+    ]
+    oracle.length = context
+    decode_engine = engine_steps[1:]
+    first = engine_steps[0][1][:1].view(1, 1).to(cuda)
+    oracle_steps = oracle_follow(oracle, first, decode_engine)
+    compare(decode_engine, oracle_steps, "32K decode")

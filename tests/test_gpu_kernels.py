@@ -311,3 +311,38 @@ def test_attention_scratch_reuse_across_shapes(ops, cuda):
         exact = _attention_fp32(q, k[:, :, :start + tokens], v[:, :, :start + tokens], mask)
         torch.testing.assert_close(out.float(), exact.transpose(1, 2).reshape(tokens, 4096), rtol=2e-2, atol=2e-2)
         assert int(tickets.abs().sum()) == 0
+
+
+def test_attention_with_too_few_splits_reports_code_204(ops, cuda):
+    """The step position lives on the device, so the host cannot check that
+    splits x chunk covers it: the kernel records code 204 instead of leaving
+    the tail out silently, and a covering launch afterwards is clean."""
+
+    from layer_streaming import _native
+
+    length = 300
+    kc, vc, k, v = _cache_with_rope(length, length + 64, 60, cuda)
+    q = randn((1, 32, 1, 128), 61).view(4096)
+    pos = torch.tensor([length - 1], dtype=torch.int32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    lib = _native.lib()
+    lib.cb_set_error_word(err.data_ptr())
+    try:
+        out = torch.empty(4096, dtype=BF16, device=cuda)
+        splits, chunk = 2, 128  # covers 256 of the 300 visible positions
+        ws = torch.empty(ops.attention_workspace_bytes(1, splits), dtype=torch.uint8, device=cuda)
+        tickets = torch.zeros(8, dtype=torch.int32, device=cuda)
+        ops.attention(q, kc, vc, pos, splits, chunk, out, ws, tickets)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 204
+        assert int(tickets.abs().sum()) == 0
+        err.zero_()
+        splits, chunk = 3, 128
+        ws = torch.empty(ops.attention_workspace_bytes(1, splits), dtype=torch.uint8, device=cuda)
+        ops.attention(q, kc, vc, pos, splits, chunk, out, ws, tickets)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        sdpa = lo.attention(q.view(1, 32, 1, 128), k, v, causal=False).view(4096)
+        torch.testing.assert_close(out.float(), sdpa.float(), rtol=2e-2, atol=2e-2)
+    finally:
+        lib.cb_set_error_word(None)

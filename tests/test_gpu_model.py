@@ -16,14 +16,12 @@ rather than to a per-element 2e-2 that the reference fails against itself;
 the per-element tolerance is checked per layer (kernel tests, smoke).
 """
 
-import json
-
 import pytest
 import torch
 from safetensors.torch import load_file
 
 import parity
-from conftest import golden_path
+from conftest import Config, engine_weights, golden_path, make_store
 from oracle import llama_oracle as lo
 from oracle.seeded import prompt_ids
 
@@ -32,61 +30,9 @@ pytestmark = pytest.mark.gpu
 RTOL = ATOL = 2e-2
 
 
-class Config:
-    hidden_size = 4096
-    intermediate_size = 14336
-    num_hidden_layers = 32
-    num_attention_heads = 32
-    num_key_value_heads = 8
-    vocab_size = 128256
-    rms_norm_eps = 1e-5
-    rope_parameters = {
-        "rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
-        "original_max_position_embeddings": 8192, "rope_theta": 500000.0,
-    }
-
-
-@pytest.fixture(scope="module")
-def meta():
-    return json.load(open(golden_path("config0.json")))
-
-
 @pytest.fixture(scope="module")
 def golden():
     return load_file(golden_path("config0.safetensors"))
-
-
-@pytest.fixture(scope="module")
-def arena(cuda, meta):
-    """One pinned, seeded host arena (its layout is the same for every plan)."""
-
-    import layer_streaming as ls
-
-    plan = ls.build_llama31_8b_plan("matrix_group")
-    store = ls.create_weight_store(plan, "full_pinned")
-    store.fill_seeded(seed=meta["weight_seed"], device=cuda)
-    return store
-
-
-def make_store(arena, plan):
-    import layer_streaming as ls
-
-    store = ls.create_weight_store(plan, "full_pinned", allocate=False)
-    assert plan.host_arena_elements == arena.plan.host_arena_elements
-    store.arena = arena.arena
-    store._loaded = True
-    return store
-
-
-@pytest.fixture(scope="module")
-def hbm_engine(cuda, arena):
-    import layer_streaming as ls
-
-    plan = ls.build_llama31_8b_plan("matrix_group")
-    store = make_store(arena, plan)
-    resident = ls.ResidentDeviceArena(plan, store, cuda)
-    runtime = ls.DoubleBufferRuntime(plan, store, resident, cuda, weights="hbm")
-    return plan, store, resident, runtime
 
 
 def generate(executor, runtime, ids, steps):
@@ -113,11 +59,7 @@ def reference_gpu_topk(cuda, hbm_engine, meta):
     """Top-k values of the reference's PyTorch ops on this GPU (the oracle's
     restatement on the same device weights), fed the golden run's inputs."""
 
-    plan, store, resident, runtime = hbm_engine
-    weights = dict(resident.views)
-    for index in range(len(plan.units)):
-        weights.update(runtime.unit_views(index))
-    return parity.reference_gpu_topk(weights, meta, cuda)
+    return parity.reference_gpu_topk(engine_weights(hbm_engine), meta, cuda)
 
 
 def check_against_golden(results, meta, gpu_topk, free_running=False):
@@ -162,10 +104,7 @@ def test_config0_parity_with_reference(cuda, hbm_engine, meta, golden, reference
     import layer_streaming as ls
 
     plan, store, resident, runtime = hbm_engine
-    weights = dict(resident.views)
-    for index in range(len(plan.units)):
-        weights.update(runtime.unit_views(index))
-    oracle = lo.OracleDecoder(weights, top_k=meta["top_k"])
+    oracle = lo.OracleDecoder(engine_weights(hbm_engine), top_k=meta["top_k"])
     executor = ls.Llama31DecodeExecutor(Config(), resident, top_k=meta["top_k"], return_full_logits=True)
     results = []
     with torch.inference_mode():
@@ -202,6 +141,13 @@ def test_config0_greedy_generation(cuda, hbm_engine, meta, reference_gpu_topk):
     executor = ls.Llama31DecodeExecutor(Config(), resident, top_k=meta["top_k"])
     ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
     results = generate(executor, runtime, ids, 1 + meta["decode_steps"])
+    engine_ids = [int(indices[0]) for _, indices, _ in results]
+    print("greedy ids, engine:    {}".format(engine_ids))
+    print("greedy ids, reference: {}".format(meta["greedy_ids"][:len(engine_ids)]))
+    for step, ((values, _, _), record) in enumerate(zip(results, meta["steps"])):
+        print("step {}: top-1/top-2 gap engine {:.4f}, reference {:.4f} (tolerance {:.4f})".format(
+            step, float(values[0] - values[1]), record["topk_values"][0] - record["topk_values"][1],
+            parity.tolerance(record["topk_values"][0])))
     check_against_golden(results, meta, reference_gpu_topk, free_running=True)
 
 

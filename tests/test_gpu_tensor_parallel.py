@@ -19,6 +19,7 @@ import json
 import os
 import subprocess
 import sys
+import time
 
 import pytest
 import torch
@@ -181,6 +182,74 @@ def test_exchange_arguments_are_validated(cuda):
             assert rc != 0, (rank, world, slot, slots)
     finally:
         lib.cb_exchange_free(own)
+
+
+def test_exchange_wait_runs_out_and_reports(ops, cuda):
+    """Failure detection of the fused exchanges on one GPU, without a fault:
+    a world of two whose second "peer" is a local exchange buffer that no
+    kernel writes. With a 1 ms limit the projection gives up, records code
+    120 (the LM head's gather 121) and returns; the same buffers then serve a
+    normal launch, bit-identical to the local kernel."""
+
+    from layer_streaming import _native
+
+    lib = _native.lib()
+    own, single = _exchange(lib, _native)
+    ghost, _ = _exchange(lib, _native)
+    pair = (ctypes.c_void_p * 2)(own.value, ghost.value)
+    stream = _native.stream_ptr(cuda)
+    epoch = torch.zeros(1, dtype=torch.int32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    x = randn((4096,), 140)
+    w = randn((4096, 4096), 141, 0.02)
+    res = randn((4096,), 142)
+    h = randn((4096,), 143)
+    head = randn((16384, 4096), 144, 0.02)
+    ws = torch.empty(ops.lm_head_workspace_bytes(10), dtype=torch.uint8, device=cuda)
+    ticket = torch.zeros(1, dtype=torch.int32, device=cuda)
+    values = torch.empty(10, dtype=torch.float32, device=cuda)
+    indices = torch.empty(10, dtype=torch.int64, device=cuda)
+    lib.cb_set_error_word(err.data_ptr())
+    previous = lib.cb_set_exchange_wait_ns(1_000_000)
+    try:
+        assert previous == 2_000_000_000
+        out = res.clone()
+        torch.cuda.synchronize()
+        started = time.perf_counter()
+        _native.check(lib.cb_proj_allreduce_residual(
+            x.data_ptr(), 4096, w.data_ptr(), 4096, out.data_ptr(), out.data_ptr(), pair, 0, 2, 0, 66,
+            epoch.data_ptr(), stream), "cb_proj_allreduce_residual")
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - started
+        assert int(err.item()) == 120
+        assert elapsed < 1.0, elapsed  # one limit per waiting thread, not per awaited word
+        err.zero_()
+        _native.check(lib.cb_lm_head_topk_allgather(
+            h.data_ptr(), None, 1e-5, head.data_ptr(), 16384, 0, 10, values.data_ptr(), indices.data_ptr(),
+            ws.data_ptr(), ticket.data_ptr(), pair, 0, 2, 1, 66, epoch.data_ptr(), stream),
+            "cb_lm_head_topk_allgather")
+        torch.cuda.synchronize()
+        assert int(err.item()) == 121
+        assert int(ticket.item()) == 0
+    finally:
+        lib.cb_set_exchange_wait_ns(0)
+    try:
+        # the next step on the same buffers (world of one) is clean and exact
+        err.zero_()
+        ops.position_advance(epoch, 1)
+        want = torch.empty_like(res)
+        ops.proj_residual(x, w, res, want)
+        out = res.clone()
+        _native.check(lib.cb_proj_allreduce_residual(
+            x.data_ptr(), 4096, w.data_ptr(), 4096, out.data_ptr(), out.data_ptr(), single, 0, 1, 0, 66,
+            epoch.data_ptr(), stream), "cb_proj_allreduce_residual")
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+        assert int(err.item()) == 0
+    finally:
+        lib.cb_set_error_word(None)
+        lib.cb_exchange_free(own)
+        lib.cb_exchange_free(ghost)
 
 
 class Config:
