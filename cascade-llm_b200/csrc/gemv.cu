@@ -64,11 +64,6 @@ __global__ void __launch_bounds__(kThreads, CB_GEMV_CTAS_PER_SM) gemv_kernel(con
 }  // namespace cb
 
 // ====================================================================== host
-#define CB_REQUIRE(cond, ...)                             \
-  do {                                                    \
-    if (!(cond)) return fail(kErrInvalid, __VA_ARGS__);   \
-  } while (0)
-
 namespace cb {
 
 int32_t* error_word();

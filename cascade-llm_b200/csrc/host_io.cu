@@ -6,7 +6,9 @@
 //                        into host memory (safetensors tensor data -> the
 //                        packed arena, weight_store.py:109-171 of the
 //                        reference reads each tensor through torch)
-// No CUDA calls: these run on any host thread, including the stores' workers.
+//   cb_host_gather_rows  embedding rows of a host table gathered into a
+//                        pinned staging buffer (vocab.py:100-131)
+// No CUDA calls: these run on any host thread, including the stager.
 #include <fcntl.h>
 #include <unistd.h>
 
@@ -36,7 +38,9 @@ int clamp_threads(int threads, int64_t tasks) {
 
 }  // namespace
 
-extern "C" int cb_host_copy(void* dst, const void* src, int64_t bytes, int threads) {
+namespace cb {
+
+int host_copy_parallel(void* dst, const void* src, int64_t bytes, int threads) {
   if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fail(kErrInvalid, "cb_host_copy: bad arguments");
   if (bytes == 0) return kOk;
   const int64_t tasks = (bytes + kCopyChunk - 1) / kCopyChunk;
@@ -57,6 +61,27 @@ extern "C" int cb_host_copy(void* dst, const void* src, int64_t bytes, int threa
   for (int i = 1; i < n; ++i) pool.emplace_back(work);
   work();
   for (auto& t : pool) t.join();
+  return kOk;
+}
+
+}  // namespace cb
+
+extern "C" int cb_host_copy(void* dst, const void* src, int64_t bytes, int threads) {
+  return host_copy_parallel(dst, src, bytes, threads);
+}
+
+// Rows ids[0..n) of a row-major host table (row_bytes each) gathered into
+// consecutive rows of dst; ids outside [0, rows) are rejected before any copy.
+extern "C" int cb_host_gather_rows(void* dst, const void* table, int64_t rows, int64_t row_bytes,
+                                   const int64_t* ids, int64_t n) {
+  CB_REQUIRE(n >= 0 && row_bytes > 0 && rows > 0, "cb_host_gather_rows: bad sizes");
+  CB_REQUIRE(n == 0 || (dst && table && ids), "cb_host_gather_rows: null pointer");
+  for (int64_t i = 0; i < n; ++i)
+    CB_REQUIRE(ids[i] >= 0 && ids[i] < rows, "cb_host_gather_rows: id %lld outside [0, %lld)", (long long)ids[i],
+               (long long)rows);
+  for (int64_t i = 0; i < n; ++i)
+    std::memcpy(static_cast<char*>(dst) + i * row_bytes, static_cast<const char*>(table) + ids[i] * row_bytes,
+                size_t(row_bytes));
   return kOk;
 }
 

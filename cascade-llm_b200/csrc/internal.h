@@ -9,6 +9,13 @@
 #include <cstdio>
 #include <string>
 
+// Argument check of a C-ABI entry point: records the message and returns
+// CB_ERR_INVALID before anything is launched.
+#define CB_REQUIRE(cond, ...)                                 \
+  do {                                                        \
+    if (!(cond)) return ::cb::fail(::cb::kErrInvalid, __VA_ARGS__); \
+  } while (0)
+
 namespace cb {
 
 // Error codes returned by every cb_* entry point.

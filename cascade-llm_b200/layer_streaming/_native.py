@@ -76,6 +76,14 @@ _SIGNATURES = {
     "cb_attention": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "cb_attention_noalloc": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _P, _P]),
     "cb_memcpy_h2d_async": (_I, [_P, _P, _I64, _P]),
+    "cb_host_gather_rows": (_I, [_P, _P, _I64, _I64, _P, _I64]),
+    "cb_ring_create": (_I, [_I, _PP, _I64, _P, _PP, _I64, _I, _PP]),
+    "cb_ring_destroy": (_I, [_P]),
+    "cb_ring_begin": (_I, [_P, _I, _PP, ctypes.POINTER(_I64), _P, _P, _I]),
+    "cb_ring_acquire": (_I, [_P, _I, _PP]),
+    "cb_ring_release": (_I, [_P, _I]),
+    "cb_ring_end": (_I, [_P, _I, ctypes.POINTER(ctypes.c_double)]),
+    "cb_ring_abort": (_I, [_P]),
 }
 
 

@@ -289,6 +289,44 @@ int cb_lm_head_topk_allgather(const void* x, const void* norm_w, float eps, cons
 int cb_host_copy(void* dst, const void* src, int64_t bytes, int threads);
 int cb_read_file_ranges(const char* path, int n, const int64_t* offsets, void* const* dsts, const int64_t* sizes,
                         int threads);
+/* Embedding rows ids[0..n) of a row-major host table ([rows, row_bytes])
+ * gathered into consecutive rows of host memory dst (the pinned staging rows
+ * of the streamed-vocabulary embedding, vocab.py:100-131); ids outside
+ * [0, rows) fail before any copy. */
+int cb_host_gather_rows(void* dst, const void* table, int64_t rows, int64_t row_bytes, const int64_t* ids,
+                        int64_t n);
+
+/* ------------------------------------------------------ streamed weights */
+
+/* Slot ring: the H2D pipeline of the streamed mode (DoubleBufferRuntime.run,
+ * layer_streaming/runtime.py:137-268, and the LM-head chunks of
+ * VocabStreamingRuntime.lm_head_topk, vocab.py:207-266). `slots` device
+ * buffers of slot_bytes are filled from host spans on `copy_stream` while a
+ * compute stream consumes them: span i lands in slot i % slots, and span
+ * i + slots is copied once the compute stream has released span i.
+ * staging (NULL, or `slots` pinned host buffers of staging_bytes): the
+ * spans are pageable; a native stager thread copies each span into a
+ * staging buffer (copy_threads threads; 0 = up to 16) once the DMA that last
+ * read that buffer has finished, then starts its H2D copy.
+ * Per pass: cb_ring_begin (orders both streams after the coordinator's
+ * queued work and starts the first `slots` copies), then for each span i in
+ * order cb_ring_acquire (compute stream waits for the copy; returns the
+ * slot's device pointer) and cb_ring_release (after the span's compute work
+ * was enqueued), then cb_ring_end (the coordinator waits for the last
+ * release and the host for the coordinator). stats (8 doubles, may be NULL):
+ * pass ms, sum of copy ms, sum of compute ms (the three with profile = 1),
+ * host ms spent waiting for copies to be issued, staging copies, their ms
+ * sum and max, bytes moved. cb_ring_abort ends a pass cut short. One pass at
+ * a time per ring; calls from one host thread. */
+int cb_ring_create(int slots, void* const* device_slots, int64_t slot_bytes, void* copy_stream,
+                   void* const* staging, int64_t staging_bytes, int copy_threads, void** ring_out);
+int cb_ring_destroy(void* ring);
+int cb_ring_begin(void* ring, int spans, const void* const* sources, const int64_t* bytes, void* compute_stream,
+                  void* coordinator_stream, int profile);
+int cb_ring_acquire(void* ring, int span, void** device_ptr);
+int cb_ring_release(void* ring, int span);
+int cb_ring_end(void* ring, int last_span, double* stats);
+int cb_ring_abort(void* ring);
 
 /* ---------------------------------------------------------------- copies */
 

@@ -246,3 +246,74 @@ def test_slot_reuse_waits_for_compute(cuda, arena, meta):
             state_ids = state.topk_indices[..., 0]
     for (v1, i1, _), (v2, i2) in zip(base, slow):
         assert torch.equal(v1, v2) and torch.equal(i1, i2)
+
+
+def test_pinned_staging_store_end_to_end(cuda, arena, hbm_engine, meta):
+    """The reference's pinned_staging mode on the GPU: a PAGEABLE host arena
+    plus two pinned staging buffers (and two pinned LM-head chunk buffers);
+    the slot ring's native stager copies every unit into a staging buffer
+    before its DMA. Same bits as the HBM-resident engine; the profile reports
+    the staging copies and the H2D rate next to the full-pinned mode's."""
+
+    import layer_streaming as ls
+
+    plan = ls.build_llama31_8b_plan("matrix_group", stream_vocab=True)
+
+    def pageable(elements, dtype=None, device=None, pin_memory=False):
+        return torch.empty(elements, dtype=dtype, device=device, pin_memory=pin_memory)
+
+    store = ls.create_weight_store(plan, "pinned_staging", tensor_factory=pageable)
+    assert not store.arena.is_pinned() and all(s.is_pinned() for s in store.staging_slots)
+    store.arena.copy_(arena.arena)
+    resident = ls.ResidentDeviceArena(plan, store, cuda)
+    runtime = ls.DoubleBufferRuntime(plan, store, resident, cuda, profile=True)
+    vocab = ls.VocabStreamingRuntime(plan, store, runtime, profile=True)
+    assert vocab.extra_pinned_cpu_bytes == 256 * 4096 * 2 + 2 * plan.vocab.chunk_elements * 2
+    executor = ls.Llama31DecodeExecutor(Config(), resident, vocab_runtime=vocab, top_k=meta["top_k"],
+                                        return_full_logits=True)
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    staged = generate(executor, runtime, ids, 3)
+    profile = runtime.last_profile
+    print("pinned_staging: {:.1f} GB/s H2D, {} staging copies ({:.1f} ms, max {:.1f}), source wait {:.1f} ms, "
+          "pipeline {:.1f} ms; LM head {:.1f} GB/s".format(
+              profile["h2d_effective_gbps"], profile["staging_copy_count"], profile["staging_event_sum_ms"],
+              profile["staging_event_max_ms"], profile["source_wait_ms"], profile["gpu_pipeline_ms"],
+              vocab.last_profile["h2d_effective_gbps"]))
+    assert profile["staging_copy_count"] == len(plan.units)
+    assert profile["h2d_bytes"] == plan.stream_bytes_per_token
+
+    _, _, hbm_resident, hbm_runtime = hbm_engine
+    hbm = ls.Llama31DecodeExecutor(Config(), hbm_resident, top_k=meta["top_k"], return_full_logits=True)
+    resident_run = generate(hbm, hbm_runtime, ids, 3)
+    for (v1, i1, l1), (v2, i2, l2) in zip(staged, resident_run):
+        assert torch.equal(v1, v2) and torch.equal(i1, i2) and torch.equal(l1, l2)
+    store.close()
+
+
+def test_streamed_pass_recovers_after_a_failing_unit(cuda, arena, meta):
+    """A compute callback that raises mid-pass: the slot ring drops the
+    queued copies, waits for the started ones and serves the next pass."""
+
+    import layer_streaming as ls
+
+    plan = ls.build_llama31_8b_plan("matrix_group")
+    store = make_store(arena, plan)
+    resident = ls.ResidentDeviceArena(plan, store, cuda)
+    runtime = ls.DoubleBufferRuntime(plan, store, resident, cuda)
+    executor = ls.Llama31DecodeExecutor(Config(), resident, top_k=meta["top_k"])
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    want = generate(executor, runtime, ids, 1)
+
+    class Boom(Exception):
+        pass
+
+    def failing(unit, weights, state):
+        if unit.layer_index == 3:
+            raise Boom()
+        return state
+
+    with pytest.raises(Boom):
+        runtime.run(failing, None)
+    again = ls.Llama31DecodeExecutor(Config(), resident, top_k=meta["top_k"])
+    got = generate(again, runtime, ids, 1)
+    assert torch.equal(want[0][0], got[0][0]) and torch.equal(want[0][1], got[0][1])

@@ -135,3 +135,36 @@ def test_unallocated_store_raises():
     store = FullPinnedWeightStore(tiny_plan(), allocate=False)
     with pytest.raises(RuntimeError):
         store.tensor("stream.weight")
+
+
+def test_native_row_gather_and_out_of_range_ids():
+    """cb_host_gather_rows: the streamed-vocabulary embedding's host gather."""
+
+    from layer_streaming import _native
+
+    lib = _native.load_library()
+    table = torch.arange(40, dtype=torch.float32).view(10, 4).to(torch.bfloat16)
+    ids = torch.tensor([3, 0, 9, 3], dtype=torch.int64)
+    out = torch.zeros(4, 4, dtype=torch.bfloat16)
+    assert lib.cb_host_gather_rows(out.data_ptr(), table.data_ptr(), 10, 8, ids.data_ptr(), 4) == 0
+    assert torch.equal(out, table[ids])
+    bad = torch.tensor([2, 10], dtype=torch.int64)
+    out.zero_()
+    assert lib.cb_host_gather_rows(out.data_ptr(), table.data_ptr(), 10, 8, bad.data_ptr(), 2) != 0
+    assert b"outside" in lib.cb_last_error()
+    assert int(out.abs().sum()) == 0  # rejected before any copy
+
+
+def test_staging_worker_reports_copy_failures():
+    plan = tiny_plan()
+    store = PinnedStagingWeightStore(plan, tensor_factory=RecordingFactory())
+
+    class BrokenEvent:
+        def synchronize(self):
+            raise RuntimeError("the DMA failed")
+
+    with pytest.raises(RuntimeError, match="DMA failed"):
+        store.prepare_unit(plan.units[0], 1, reuse_event=BrokenEvent()).result()
+    # the worker survives and serves the next request
+    assert store.prepare_unit(plan.units[0], 0).result().numel() == 4
+    store.close()
