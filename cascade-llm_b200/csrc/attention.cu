@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
   uint64_t* empty = full + kAttnStages;
   uint8_t* scratch = smem + AttnSmem::SCR_OFF;
 
+  const uint64_t t0 = trace_now(p.trace);
   const int s = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   int64_t pos0, start, stop;
@@ -106,6 +107,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
   // would otherwise stream weights during this kernel's latency-bound
   // publish/merge and slow it (decode step 3.37 -> 3.12 ms measured).
   grid_dep_wait();
+  const uint64_t t1 = trace_now(p.trace);
   uint64_t qd[kGroup][4];
   attn_load_q(p, m, g, qd);
   AttnWarpState ws;
@@ -126,7 +128,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
       phase ^= 1;
     }
   }
+  const uint64_t t2 = trace_now(p.trace);
   attn_publish(p, s, g, m, pos0, ws, scratch, reinterpret_cast<float*>(ks), ConsumerSync());
+  if (tid == 0)
+    trace_commit(p.trace, p.trace_tag, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x, t0, t1, t2);
 }
 
 int prepare_attention() { return configure_smem("cb_attention", attention_kernel, AttnSmem::BYTES); }
@@ -172,6 +177,7 @@ extern "C" int cb_attention(const void* q, const void* k_cache, const void* v_ca
   p.part_ml = reinterpret_cast<float*>(ws + rows * kHeadDim * 4);
   p.tickets = tickets;
   p.err = error_word();
+  p.trace = trace_buffer(&p.trace_tag);
   return launch("cb_attention", attention_kernel, dim3(splits, kv_heads, M), dim3(kAttnThreads),
                 AttnSmem::BYTES, static_cast<cudaStream_t>(stream), p);
 }

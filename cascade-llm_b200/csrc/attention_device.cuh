@@ -28,6 +28,8 @@ struct AttnParams {
   float* part_ml;            // [M][kv_heads * 4][splits][2]
   unsigned int* tickets;     // [M][kv_heads]
   int* err;
+  uint64_t* trace;           // per-CTA timeline (cb_set_trace) or null
+  uint32_t trace_tag;
 };
 
 constexpr int kRowsPerWarp = kSub / kAttnWarps;  // 8 rows of a sub-chunk per warp

@@ -157,6 +157,33 @@ __device__ __forceinline__ uint32_t wait_tagged(const uint64_t* p, uint32_t tag,
   return uint32_t(w);
 }
 
+// ------------------------------------------------------- launch tracing
+// Optional per-CTA timeline of the engine's kernels (cb_set_trace): buffer
+// word 0 is the record cursor, word 1 the capacity in records; record r
+// (8 words at 8 * (r + 1)) holds the launch tag << 32 | CTA index, the SM,
+// and %globaltimer at CTA start, after the dependency wait, after the main
+// loop and at the end. A null buffer (the default) records nothing.
+__device__ __forceinline__ uint32_t smid_u32() {
+  uint32_t v;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(v));
+  return v;
+}
+__device__ __forceinline__ uint64_t trace_now(const uint64_t* trace) { return trace ? globaltimer_ns() : 0; }
+__device__ __forceinline__ void trace_commit(uint64_t* trace, uint32_t tag, uint32_t cta, uint64_t t0, uint64_t t1,
+                                             uint64_t t2) {
+  if (!trace) return;
+  const uint64_t t3 = globaltimer_ns();
+  const unsigned long long slot = atomicAdd(reinterpret_cast<unsigned long long*>(trace), 1ull);
+  if (slot >= trace[1]) return;
+  uint64_t* r = trace + 8 * (slot + 1);
+  r[0] = (uint64_t(tag) << 32) | cta;
+  r[1] = smid_u32();
+  r[2] = t0;
+  r[3] = t1;
+  r[4] = t2;
+  r[5] = t3;
+}
+
 // ------------------------------------------------------------ loads/stores
 // Activations written by an earlier kernel are read through L2 only (.cg):
 // with overlapping dependent launches no stale L1 line can be hit.

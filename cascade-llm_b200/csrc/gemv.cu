@@ -54,11 +54,17 @@ static int lm_head_grid() { return gemv_grid(); }
 template <int K>
 __global__ void __launch_bounds__(kThreads, CB_GEMV_CTAS_PER_SM) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t times[3];  // launch trace: start, after the wait, after the main loop
+  if (p.trace && threadIdx.x == 0) times[0] = globaltimer_ns();
   GemvRegs<K, CB_GEMV_DEPTH> r;
   gemv_prefetch<K, CB_GEMV_DEPTH>(p, blockIdx.x, gridDim.x, r);
   grid_dep_wait();  // the activation row comes from the previous kernel
-  if (threadIdx.x == 0) grid_dep_launch();
-  gemv_run<K, CB_GEMV_DEPTH>(p, smem, blockIdx.x, gridDim.x, r);
+  if (threadIdx.x == 0) {
+    if (p.trace) times[1] = globaltimer_ns();
+    grid_dep_launch();
+  }
+  gemv_run<K, CB_GEMV_DEPTH>(p, smem, blockIdx.x, gridDim.x, r, p.trace ? &times[2] : nullptr);
+  if (p.trace && threadIdx.x == 0) trace_commit(p.trace, p.trace_tag, blockIdx.x, times[0], times[1], times[2]);
 }
 
 }  // namespace cb
@@ -72,6 +78,7 @@ int finish_params(GemvParams& p) {
   p.total_units = 0;
   for (int i = 0; i < p.nseg; ++i) p.total_units += p.seg[i].units;
   p.err = error_word();
+  p.trace = trace_buffer(&p.trace_tag);
   return kOk;
 }
 

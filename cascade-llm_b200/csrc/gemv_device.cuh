@@ -95,6 +95,8 @@ struct GemvParams {
   int slot, slots;
   const int32_t* epoch;    // device step counter, advanced once per step
   uint64_t wait_ns;        // how long a peer's word is awaited before the launch gives up
+  uint64_t* trace;         // per-CTA timeline (cb_set_trace) or null
+  uint32_t trace_tag;
 };
 
 __device__ __forceinline__ int64_t unit_row(const Segment& s, int j) {
@@ -461,7 +463,8 @@ __device__ __forceinline__ void gemv_prefetch(const GemvParams& p, int cta, int 
 // The activation slice of a warp stays in registers. `r` holds the first
 // batch issued by gemv_prefetch. Requires the activation row to be complete.
 template <int K, int DEPTH = 1>
-static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int ncta, GemvRegs<K, DEPTH>& r) {
+static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int ncta, GemvRegs<K, DEPTH>& r,
+                                uint64_t* t_loop = nullptr) {
   using S = GemvShape<K, DEPTH>;
   float* red = reinterpret_cast<float*>(smem + S::RED);
   float* part = reinterpret_cast<float*>(smem + S::SMEM);  // [units][2][WARPS]
@@ -567,6 +570,7 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
     consume(r, ub);
   }
   __syncthreads();
+  if (t_loop && tid == 0) *t_loop = trace_now(p.trace);
 
   for (int i = tid; i < units; i += kThreads) {
     float a = 0.f, b = 0.f;

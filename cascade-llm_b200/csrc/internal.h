@@ -33,6 +33,9 @@ bool pdl_enabled();
 // Wall-clock limit of the tensor-parallel exchange waits (cb_set_exchange_wait_ns).
 uint64_t exchange_wait_ns();
 int sm_count();
+// The launch-trace buffer set by cb_set_trace (null: tracing off) and, when
+// set, the next launch tag.
+uint64_t* trace_buffer(uint32_t* tag);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -42,6 +42,13 @@ int check_launch(const char* what) {
 bool pdl_enabled() { return g_pdl; }
 uint64_t exchange_wait_ns() { return g_exchange_wait_ns.load(); }
 
+static uint64_t* g_trace = nullptr;
+static std::atomic<uint32_t> g_trace_tag{0};
+uint64_t* trace_buffer(uint32_t* tag) {
+  if (g_trace && tag) *tag = g_trace_tag.fetch_add(1);
+  return g_trace;
+}
+
 int sm_count() {
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -218,6 +225,11 @@ extern "C" int cb_set_pdl(int enable) {
   const int prev = g_pdl ? 1 : 0;
   g_pdl = enable != 0;
   return prev;
+}
+extern "C" int cb_set_trace(void* device_buffer) {
+  g_trace = static_cast<uint64_t*>(device_buffer);
+  g_trace_tag = 0;
+  return kOk;
 }
 extern "C" uint64_t cb_set_exchange_wait_ns(uint64_t ns) {
   return g_exchange_wait_ns.exchange(ns ? ns : 2000000000ull);

@@ -34,6 +34,7 @@ _SIGNATURES = {
     "cb_sm_count": (_I, []),
     "cb_prepare": (_I, []),
     "cb_set_error_word": (_I, [_P]),
+    "cb_set_trace": (_I, [_P]),
     "cb_stream_key": (ctypes.c_uint64, [ctypes.c_uint64, ctypes.c_char_p]),
     "cb_fill_normal_bf16": (_I, [_P, _I64, _I64, ctypes.c_uint64, ctypes.c_double, _P]),
     "cb_fill_bf16": (_I, [_P, _I64, _F, _P]),

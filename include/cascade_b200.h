@@ -45,6 +45,15 @@ int cb_prepare(void);
  * instead of hanging or faulting. NULL disables the reporting. One word per
  * process (one process per GPU). The host reads it between steps. */
 int cb_set_error_word(int32_t* device_word);
+/* Per-CTA launch timeline of the decode kernels, for profiling: launches
+ * issued while a buffer is set append one record per CTA (u64 words: the
+ * buffer's word 0 is the record count, to be zeroed by the caller, word 1 the
+ * capacity in records; record r is the 8 words at 8 * (r + 1): launch tag
+ * << 32 | CTA index, SM id, and %globaltimer ns at CTA start, after the
+ * dependency wait, after the main loop, at the end). Launch tags count up
+ * from 0 per cb_set_trace call, in issue order (a captured graph replays its
+ * tags). NULL (the default) turns tracing off. */
+int cb_set_trace(void* device_buffer);
 
 /* ---------------------------------------------------------------- set-up */
 
