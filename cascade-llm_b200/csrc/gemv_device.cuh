@@ -20,7 +20,7 @@ enum EpiMode : int {
 
 constexpr int kThreads = 256;
 constexpr int kTopkMax = 64;
-constexpr size_t kMaxSmem = 227 * 1024;
+constexpr size_t kMaxSmem = 226 * 1024;  // dynamic; the kernels also hold a little static shared memory
 
 // Tensor-parallel exchange buffer of one rank (device memory that every rank
 // maps; the same layout on all ranks). Every entry is a tagged 64-bit word
