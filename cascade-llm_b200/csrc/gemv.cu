@@ -94,7 +94,9 @@ static int run_gemv(const char* what, GemvParams& p, cudaStream_t stream) {
   size_t smem = S::SMEM + per_cta * 2 * S::WK * sizeof(float);  // per-unit partials
   if (p.cand_values) {
     // EPI_TOPK: the CTA's logits, later reused as the last CTA's merge scratch
-    smem += std::max(per_cta * 2 * sizeof(float), size_t(kMergeCap) * (sizeof(float) + sizeof(int64_t)));
+    // logits -> keys of this CTA's rows and the selection stage; the last CTA
+    // reuses the region for the merge of all CTAs' candidates
+    smem += std::max(per_cta * 2 * sizeof(float) + size_t(kThreads / 32) * kTopkMax * 8, kTopkScratchBytes);
   }
   if (smem > kMaxSmem) return fail(kErrInvalid, "%s: %zu units per CTA exceed shared memory", what, per_cta);
   return launch(what, gemv_kernel<K>, dim3(grid), dim3(kThreads), smem, stream, p);
@@ -367,6 +369,8 @@ static int build_lm_head_params(GemvParams& p, const void* x, const void* norm_w
   CB_REQUIRE(rows > 0 && rows % 2 == 0 && rows <= (int64_t(1) << 30),
              "cb_lm_head_topk: rows must be even, positive and < 2^30 (got %lld)", (long long)rows);
   CB_REQUIRE(k >= 1 && k <= kTopkMax && k <= rows, "cb_lm_head_topk: need 1 <= k <= min(64, rows)");
+  CB_REQUIRE(row_offset >= 0 && row_offset + rows <= (int64_t(1) << 31),
+             "cb_lm_head_topk: row ids must fit 31 bits (row_offset + rows <= 2^31)");
   p = GemvParams{};
   p.x = static_cast<const uint16_t*>(x);
   p.norm_w = static_cast<const uint16_t*>(norm_w);

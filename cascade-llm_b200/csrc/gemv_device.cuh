@@ -107,80 +107,79 @@ __device__ __forceinline__ bool ranks_before(float va, int64_t ia, float vb, int
   return va > vb || (va == vb && ia < ib);
 }
 
-// Warp-cooperative exact top-k over n (value, index) pairs in shared memory.
-static __device__ void warp_select_rows_idx(const float* vals, const int64_t* idx, int n, int k, float* out_v,
-                                     int64_t* out_i) {
+// ------------------------------------------------------------ exact top-k
+// Order: larger value first, then smaller row id (torch.topk leaves ties
+// unspecified; this order is the engine's documented tie rule). Values are
+// compared as order-preserving 32-bit keys; key 0 marks a removed or missing
+// entry (no finite value or infinity maps to it). Row ids fit 31 bits (the
+// host checks row_offset + rows <= 2^31).
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t key) {
+  return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
+// Warp-cooperative top-k of entries [lo, hi) of `keys` (shared memory) with
+// distinct ids id_of(c): round r takes the largest key and, among equal
+// keys, the smallest id (two warp reductions), removes it from `keys` and
+// stages it at out_key[r] / out_id[r] (key 0 once the range is exhausted).
+template <class IdOf>
+__device__ __forceinline__ void warp_topk(uint32_t* keys, IdOf id_of, int lo, int hi, int k, uint32_t* out_key,
+                                          uint32_t* out_id) {
   const int lane = threadIdx.x & 31;
-  float pv = __int_as_float(0x7F800000);
-  int64_t pi = -1;
   for (int r = 0; r < k; ++r) {
-    float bv = -__int_as_float(0x7F800000);
-    int64_t bi = INT64_MAX;
-    for (int c = lane; c < n; c += 32) {
-      const float v = vals[c];
-      const int64_t i = idx[c];
-      if (ranks_before(pv, pi, v, i) && ranks_before(v, i, bv, bi)) {
-        bv = v;
-        bi = i;
+    uint32_t bk = 0u, bi = 0xFFFFFFFFu;
+    int bp = -1;
+    for (int c = lo + lane; c < hi; c += 32) {
+      const uint32_t kk = keys[c];
+      if (kk == 0u || kk < bk) continue;
+      const uint32_t ii = id_of(c);
+      if (kk > bk || ii < bi) {
+        bk = kk;
+        bi = ii;
+        bp = c;
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-      const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-      if (ranks_before(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
+    const uint32_t wk = __reduce_max_sync(0xFFFFFFFFu, bk);
+    const uint32_t wi = __reduce_min_sync(0xFFFFFFFFu, bk == wk ? bi : 0xFFFFFFFFu);
+    if (wk != 0u && bk == wk && bi == wi) keys[bp] = 0u;  // exactly one lane owns it
     if (lane == 0) {
-      out_v[r] = bv;
-      out_i[r] = bi;
+      out_key[r] = wk;
+      out_id[r] = wi;
     }
-    pv = bv;
-    pi = bi;
+    __syncwarp();
   }
 }
 
-// Warp-cooperative exact top-k over a CTA's logits in shared memory:
-// entry i < na is row a0 + i, entry i >= na is row b0 + (i - na). Missing
-// entries (n < k) are written as (-inf, INT64_MAX).
-static __device__ void warp_select_rows(const float* vals, int n, int na, int64_t a0, int64_t b0, int k,
-                                 float* out_v, int64_t* out_i) {
-  const int lane = threadIdx.x & 31;
-  float pv = __int_as_float(0x7F800000);
-  int64_t pi = -1;
-  for (int r = 0; r < k; ++r) {
-    float bv = -__int_as_float(0x7F800000);
-    int64_t bi = INT64_MAX;
-    for (int c = lane; c < n; c += 32) {
-      const float v = vals[c];
-      const int64_t i = c < na ? a0 + c : b0 + (c - na);
-      if (ranks_before(pv, pi, v, i) && ranks_before(v, i, bv, bi)) {
-        bv = v;
-        bi = i;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-      const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-      if (ranks_before(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (lane == 0) {
-      out_v[r] = bv;
-      out_i[r] = bi;
-    }
-    pv = bv;
-    pi = bi;
+// Exact top-k of n entries (keys in shared memory, ids by id_of) by the whole
+// CTA: each of the 8 warps selects the top-k of its eighth into `stage`
+// (8k keys, then 8k ids), then warp 0 selects the k best of those and writes
+// values / int64 ids to out_v / out_i (missing entries: -inf, INT64_MAX).
+template <class IdOf>
+static __device__ void block_topk(uint32_t* keys, IdOf id_of, int n, int k, uint32_t* stage, float* out_v,
+                                  int64_t* out_i) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int W = kThreads / 32;
+  uint32_t* st_key = stage;
+  uint32_t* st_id = stage + W * k;
+  warp_topk(keys, id_of, int(int64_t(n) * warp / W), int(int64_t(n) * (warp + 1) / W), k, st_key + warp * k,
+            st_id + warp * k);
+  __syncthreads();
+  if (warp != 0) return;
+  warp_topk(st_key, [st_id](int c) { return st_id[c]; }, 0, W * k, k, st_key, st_id);
+  __syncwarp();
+  for (int r = lane; r < k; r += 32) {
+    const uint32_t key = st_key[r];
+    out_v[r] = key ? key_value(key) : -__int_as_float(0x7F800000);
+    out_i[r] = key ? int64_t(st_id[r]) : INT64_MAX;
   }
 }
 
-// Warp-cooperative exact top-k of n candidates; lane 0 writes the result.
-// Round r selects the best candidate that ranks strictly after round r-1's.
+// Reference selection over candidate lists in global memory by one warp,
+// k rounds of a full scan: the fallback of block_merge_topk when more than
+// kMergeCap candidates tie at the threshold.
 static __device__ void warp_select_topk(const float* vals, const int64_t* idx, int n, int k,
                                  float* out_v, int64_t* out_i) {
   const int lane = threadIdx.x & 31;
@@ -218,50 +217,51 @@ static __device__ void warp_select_topk(const float* vals, const int64_t* idx, i
   }
 }
 
-// Exact top-k of G sorted per-CTA candidate lists (k each, in global
-// memory), by the whole CTA. The k-th best of the union is at least the
-// largest per-list k-th value, so only candidates at or above that
-// threshold can qualify: one parallel pass finds the threshold, a second
-// copies the survivors to shared memory, and warp 0 selects among them.
-// `scratch` must hold kMergeCap floats + kMergeCap int64s.
+// Exact top-k of G per-CTA candidate lists (k each, in global memory), by the
+// whole CTA. The k-th best of the union is at least the largest per-list
+// k-th value, so only candidates at or above that threshold can qualify: one
+// pass finds the threshold, a second copies the survivors (keys and ids) to
+// shared memory, and block_topk selects among them. `scratch` holds
+// kMergeCap keys, kMergeCap ids and the 8k-entry stage (12 KB).
 constexpr int kMergeCap = 1024;
+constexpr size_t kTopkScratchBytes = size_t(kMergeCap) * 8 + size_t(kThreads / 32) * kTopkMax * 8;
 static __device__ void block_merge_topk(const float* vals, const int64_t* idx, int G, int k, float* out_v,
-                                 int64_t* out_i, float* red, float* scratch) {
+                                 int64_t* out_i, float* red, uint32_t* scratch) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float thr = -__int_as_float(0x7F800000);
-  for (int c = tid; c < G; c += blockDim.x) thr = fmaxf(thr, __ldcg(vals + size_t(c) * k + (k - 1)));
-  thr = warp_max(thr);
+  uint32_t thr = 0u;
+  for (int c = tid; c < G; c += blockDim.x) thr = max(thr, order_key(__ldcg(vals + size_t(c) * k + (k - 1))));
+  thr = __reduce_max_sync(0xFFFFFFFFu, thr);
   __syncthreads();
-  if (lane == 0) red[warp] = thr;
+  uint32_t* wred = reinterpret_cast<uint32_t*>(red);
+  if (lane == 0) wred[warp] = thr;
   int* count = reinterpret_cast<int*>(red + 14);
   if (tid == 0) *count = 0;
   __syncthreads();
-  thr = red[0];
-  for (int q = 1; q < int(blockDim.x >> 5); ++q) thr = fmaxf(thr, red[q]);
-  float* sv = scratch;
-  int64_t* si = reinterpret_cast<int64_t*>(scratch + kMergeCap);
+  thr = wred[0];
+  for (int q = 1; q < int(blockDim.x >> 5); ++q) thr = max(thr, wred[q]);
+  uint32_t* keys = scratch;
+  uint32_t* ids = scratch + kMergeCap;
+  uint32_t* stage = scratch + 2 * kMergeCap;
   const int n = G * k;
   for (int c = tid; c < n; c += blockDim.x) {
-    const float v = __ldcg(vals + c);
-    if (v >= thr) {
+    const uint32_t key = order_key(__ldcg(vals + c));
+    const int64_t i = __ldcg(reinterpret_cast<const long long*>(idx) + c);
+    if (key >= thr && i != INT64_MAX) {
       const int slot = atomicAdd(count, 1);
       if (slot < kMergeCap) {
-        sv[slot] = v;
-        si[slot] = __ldcg(reinterpret_cast<const long long*>(idx) + c);
+        keys[slot] = key;
+        ids[slot] = uint32_t(i);
       }
     }
   }
   __syncthreads();
   const int kept = *count;
-  if (warp == 0) {
-    if (kept <= kMergeCap)
-      warp_select_rows_idx(sv, si, kept, k, out_v, out_i);
-    else  // pathological ties: fall back to scanning every candidate
-      warp_select_topk(vals, idx, n, k, out_v, out_i);
+  if (kept <= kMergeCap) {
+    block_topk(keys, [ids](int c) { return ids[c]; }, kept, k, stage, out_v, out_i);
+  } else if (warp == 0) {  // pathological ties: scan every candidate
+    warp_select_topk(vals, idx, n, k, out_v, out_i);
   }
 }
-
-
 
 __device__ __forceinline__ uint4 normalize8(uint4 xu, uint4 wu, float inv) {
   const uint32_t in[4] = {xu.x, xu.y, xu.z, xu.w};
@@ -599,10 +599,18 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   if (p.cand_values == nullptr) return;
   // ---------------- LM head: this CTA's exact top-k, then the last CTA merges
   __syncthreads();
-  if (warp == 0) {
-    const int64_t half = p.seg[0].b_offset;
-    warp_select_rows(lrow, 2 * units, units, p.row_offset + u0, p.row_offset + half + u0, p.k,
-                     p.cand_values + size_t(cta) * p.k, p.cand_indices + size_t(cta) * p.k);
+  uint32_t* lkey = reinterpret_cast<uint32_t*>(lrow);  // the logits, as order keys in place
+  for (int i = tid; i < 2 * units; i += kThreads) lkey[i] = order_key(lrow[i]);
+  __syncthreads();
+  {
+    // entry i < units is row A of unit u0 + i, entry units + i its row B:
+    // every B row (j + N/2) follows every A row, so entry order is id order
+    const uint32_t a0 = uint32_t(p.row_offset + u0);
+    const uint32_t b0 = uint32_t(p.row_offset + p.seg[0].b_offset + u0);
+    const int na = units;
+    block_topk(lkey, [a0, b0, na](int c) { return c < na ? a0 + uint32_t(c) : b0 + uint32_t(c - na); },
+               2 * units, p.k, lkey + 2 * units, p.cand_values + size_t(cta) * p.k,
+               p.cand_indices + size_t(cta) * p.k);
   }
   __syncthreads();
   if (tid == 0) {
@@ -613,7 +621,8 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   }
   __syncthreads();
   if (__float_as_int(red[15]) != 1) return;
-  block_merge_topk(p.cand_values, p.cand_indices, ncta, p.k, p.out_values, p.out_indices, red, lrow);
+  block_merge_topk(p.cand_values, p.cand_indices, ncta, p.k, p.out_values, p.out_indices, red,
+                   reinterpret_cast<uint32_t*>(lrow));
   if (tid == 0) *p.ticket = 0u;
   if (!p.world) return;
   // ---------------- vocabulary-sharded LM head: push this rank's k
@@ -630,17 +639,18 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
     st_tagged(xchg_cand_v(p.xchg[q], par) + p.rank * k + i, tag_word(__float_as_uint(v), seq));
     st_tagged(xchg_cand_i(p.xchg[q], par) + p.rank * k + i, tag_word(row, seq));
   }
-  float* sv = lrow;  // merge scratch: kMergeCap values, then kMergeCap int64 ids
-  int64_t* si = reinterpret_cast<int64_t*>(lrow + kMergeCap);
+  uint32_t* keys = reinterpret_cast<uint32_t*>(lrow);  // gathered keys, ids, then the stage
+  uint32_t* ids = keys + kMergeCap;
   bool late = false;
   uint8_t* own = p.xchg[p.rank];
   for (int e = tid; e < p.world * k; e += kThreads) {
-    sv[e] = __uint_as_float(wait_tagged(xchg_cand_v(own, par) + e, seq, p.wait_ns, &late));
-    si[e] = int64_t(wait_tagged(xchg_cand_i(own, par) + e, seq, p.wait_ns, &late));
+    keys[e] = order_key(__uint_as_float(wait_tagged(xchg_cand_v(own, par) + e, seq, p.wait_ns, &late)));
+    ids[e] = wait_tagged(xchg_cand_i(own, par) + e, seq, p.wait_ns, &late);
   }
   if (late && p.err) atomicExch(p.err, 121);
-  __syncthreads();
-  if (warp == 0) warp_select_rows_idx(sv, si, p.world * k, k, p.out_values, p.out_indices);
+  __syncthreads();  // also: every thread has read out_values / out_indices above before they are rewritten
+  block_topk(keys, [ids](int c) { return ids[c]; }, p.world * k, k, keys + 2 * kMergeCap, p.out_values,
+             p.out_indices);
 }
 
 // Host-side parameter builders (gemv.cu).
