@@ -26,112 +26,10 @@ namespace cb {
 
 int32_t* error_word();
 
-constexpr int kAttnStages = 3;
-constexpr int kAttnThreads = kAttnConsumers + 32;  // + one producer warp
-
-struct AttnSmem {
-  static constexpr size_t STAGE = size_t(kSub) * kHeadDim * 2;  // one of K or V
-  static constexpr size_t K_OFF = 0;
-  static constexpr size_t V_OFF = K_OFF + kAttnStages * STAGE;
-  static constexpr size_t BAR_OFF = V_OFF + kAttnStages * STAGE;   // full, empty
-  static constexpr size_t SCR_OFF = BAR_OFF + 2 * kAttnStages * 8;
-  static constexpr size_t BYTES = SCR_OFF + AttnScratch::BYTES;
-  static_assert(kAttnStages * STAGE >= size_t(kAttnWarps) * kGroup * kHeadDim * 4,
-                "the K ring stages the cross-warp combine");
-  static_assert(SCR_OFF % 16 == 0, "scratch alignment");
-};
-
-struct ConsumerSync {
-  __device__ void operator()() const { named_sync(1, kAttnConsumers); }
-};
-
-// A CTA owns (split s, kv head g, token m): a producer warp streams its
-// positions in 64-position sub-chunks through a 3-stage cp.async.bulk ring;
-// rows of the history (< the step's first position) are fetched before
-// griddepcontrol.wait, rows written by this step's QKV kernel after it.
 __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint16_t* ks = reinterpret_cast<uint16_t*>(smem + AttnSmem::K_OFF);
-  uint16_t* vs = reinterpret_cast<uint16_t*>(smem + AttnSmem::V_OFF);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + AttnSmem::BAR_OFF);
-  uint64_t* empty = full + kAttnStages;
-  uint8_t* scratch = smem + AttnSmem::SCR_OFF;
-
-  const uint64_t t0 = trace_now(p.trace);
-  const int s = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-  int64_t pos0, start, stop;
-  const int nsub = attn_range(p, s, m, pos0, start, stop);
-
-  if (tid == 0) {
-    for (int i = 0; i < kAttnStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kAttnWarps);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-
-  if (warp == kAttnWarps) {
-    // ---------------- producer
-    if (lane == 0) {
-      bool waited = false;
-      int stage = 0;
-      uint32_t phase = 0;
-      const uint16_t* kbase = p.k_cache + int64_t(g) * p.cache_len * kHeadDim;
-      const uint16_t* vbase = p.v_cache + int64_t(g) * p.cache_len * kHeadDim;
-      for (int i = 0; i < nsub; ++i) {
-        const int64_t t0 = start + int64_t(i) * kSub;
-        const int rows = int(min(int64_t(kSub), stop - t0));
-        if (!waited && t0 + kSub > pos0) {  // touches rows written by this step
-          grid_dep_wait();
-          waited = true;
-        }
-        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 202)) return;
-        const uint32_t bytes = uint32_t(rows) * kHeadDim * 2;
-        mbar_arrive_expect_tx(&full[stage], 2 * bytes);
-        bulk_g2s(ks + size_t(stage) * kSub * kHeadDim, kbase + t0 * kHeadDim, bytes, &full[stage]);
-        bulk_g2s(vs + size_t(stage) * kSub * kHeadDim, vbase + t0 * kHeadDim, bytes, &full[stage]);
-        if (++stage == kAttnStages) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-    }
-    return;
-  }
-
-  // ---------------- consumers
-  // q comes from the QKV kernel. No early griddepcontrol.launch_dependents:
-  // the next kernel (o_proj) starts when this grid exits, since its CTAs
-  // would otherwise stream weights during this kernel's latency-bound
-  // publish/merge and slow it (decode step 3.37 -> 3.12 ms measured).
-  grid_dep_wait();
-  const uint64_t t1 = trace_now(p.trace);
-  uint64_t qd[kGroup][4];
-  attn_load_q(p, m, g, qd);
-  AttnWarpState ws;
-  attn_state_init(ws);
-  float* pw = reinterpret_cast<float*>(scratch + AttnScratch::PW) + warp * 80;
-  int stage = 0;
-  uint32_t phase = 0;
-  bool failed = false;  // a timed-out wait records the error; control flow is unchanged
-  for (int i = 0; i < nsub; ++i) {
-    const int64_t t0 = start + int64_t(i) * kSub;
-    const int rows = int(min(int64_t(kSub), stop - t0));
-    if (!failed && !mbar_wait(&full[stage], phase, p.err, 203)) failed = true;
-    attn_rows(ks + size_t(stage) * kSub * kHeadDim, vs + size_t(stage) * kSub * kHeadDim, rows, qd, ws, pw);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[stage]);
-    if (++stage == kAttnStages) {
-      stage = 0;
-      phase ^= 1;
-    }
-  }
-  const uint64_t t2 = trace_now(p.trace);
-  attn_publish(p, s, g, m, pos0, ws, scratch, reinterpret_cast<float*>(ks), ConsumerSync());
-  if (tid == 0)
-    trace_commit(p.trace, p.trace_tag, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x, t0, t1, t2);
+  attention_cta(p, blockIdx.x, blockIdx.y, blockIdx.z, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
+                smem);
 }
 
 int prepare_attention() { return configure_smem("cb_attention", attention_kernel, AttnSmem::BYTES); }
@@ -156,7 +54,7 @@ extern "C" int cb_attention(const void* q, const void* k_cache, const void* v_ca
     return fail(kErrInvalid, "cb_attention: q/k_cache/v_cache must be 16-byte aligned");
   if (M < 1 || M > 65535) return fail(kErrInvalid, "cb_attention: M=%d out of range", M);
   if (splits < 1 || splits > 65535) return fail(kErrInvalid, "cb_attention: splits=%d", splits);
-  if (chunk < kSub || chunk % kSub) return fail(kErrInvalid, "cb_attention: chunk must be a multiple of 64");
+  if (chunk < 0 || chunk % kSub) return fail(kErrInvalid, "cb_attention: chunk must be 0 or a multiple of 64");
   if (cache_len < 1) return fail(kErrInvalid, "cb_attention: cache_len must be positive");
   int rc = configure_smem("cb_attention", attention_kernel, AttnSmem::BYTES);
   if (rc != kOk) return rc;

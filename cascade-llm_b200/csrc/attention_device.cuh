@@ -30,6 +30,7 @@ struct AttnParams {
   int* err;
   uint64_t* trace;           // per-CTA timeline (cb_set_trace) or null
   uint32_t trace_tag;
+  unsigned int* heads_done;  // fused launches: count of merged (token, kv head) outputs, or null
 };
 
 constexpr int kRowsPerWarp = kSub / kAttnWarps;  // 8 rows of a sub-chunk per warp
@@ -46,6 +47,17 @@ struct AttnScratch {
   static constexpr size_t BYTES = MRG + (kGroup * kMergeBlock + 3 * kGroup + 4) * 4;
 };
 
+// Positions per split: p.chunk, or (p.chunk == 0) sized on the device from
+// the step's position so that the splits cover the longest context of the
+// step in whole 64-position sub-chunks (every split holds keys once the
+// context has splits x 64 positions).
+__device__ __forceinline__ int64_t attn_chunk(const AttnParams& p, int64_t pos0) {
+  if (p.chunk > 0) return p.chunk;
+  const int64_t longest = min(pos0 + p.M, p.cache_len);
+  const int64_t per = (longest + p.splits - 1) / p.splits;
+  return max(int64_t(kSub), (per + kSub - 1) / kSub * kSub);
+}
+
 // Positions [start, stop) of split s for token m, and the sub-chunk count.
 __device__ __forceinline__ int attn_range(const AttnParams& p, int s, int m, int64_t& pos0, int64_t& start,
                                           int64_t& stop) {
@@ -55,10 +67,11 @@ __device__ __forceinline__ int attn_range(const AttnParams& p, int s, int m, int
     if (threadIdx.x == 0 && p.err) atomicExch(p.err, 201);
     visible = p.cache_len;
   }
-  if (visible > int64_t(p.splits) * p.chunk && s == 0 && threadIdx.x == 0 && p.err)
+  const int64_t chunk = attn_chunk(p, pos0);
+  if (visible > int64_t(p.splits) * chunk && s == 0 && threadIdx.x == 0 && p.err)
     atomicExch(p.err, 204);  // too few splits for this position: the tail is left out
-  start = int64_t(s) * p.chunk;
-  stop = min(start + int64_t(p.chunk), visible);
+  start = int64_t(s) * chunk;
+  stop = min(start + chunk, visible);
   return start < stop ? int((stop - start + kSub - 1) / kSub) : 0;
 }
 
@@ -203,7 +216,7 @@ __device__ __forceinline__ void attn_rows(const uint16_t* kst, const uint16_t* v
 // `ring` (>= 16 KB of shared memory no longer read by any warp after
 // the first barrier) stages the rescaled o of every warp.
 template <class Sync>
-static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, int64_t pos0,
+static __device__ bool attn_publish(const AttnParams& p, int s, int g, int m, int64_t pos0,
                                     const AttnWarpState& st, uint8_t* scratch, float* ring, Sync sync) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const float ninf = -__int_as_float(0x7F800000);
@@ -256,7 +269,7 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, in
     *flag = ticket == unsigned(p.splits - 1) ? 1 : 0;
   }
   sync();
-  if (*flag == 0) return;
+  if (*flag == 0) return false;
   // Merge over the splits that hold keys for this token (a split that starts
   // past its last visible position has weight 0), kMergeBlock splits per
   // round trip: every (m, l) pair and every o value of the block is loaded
@@ -266,7 +279,8 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, in
     st_L[tid] = 0.f;
   }
   const int64_t visible = min(pos0 + m + 1, p.cache_len);
-  const int live = max(1, min(p.splits, int((visible + p.chunk - 1) / p.chunk)));
+  const int64_t chunk = attn_chunk(p, pos0);
+  const int live = max(1, min(p.splits, int((visible + chunk - 1) / chunk)));
   const int64_t grp = int64_t(m) * p.kv_heads * kGroup + g * kGroup;  // first (token, head) row
   float acc[2] = {0.f, 0.f};
   const int h0 = tid / kHeadDim, h1 = (tid + kAttnConsumers) / kHeadDim, d0 = tid % kHeadDim;
@@ -313,6 +327,121 @@ static __device__ void attn_publish(const AttnParams& p, int s, int g, int m, in
   out[h0 * kHeadDim + d0] = f2bf(acc[0] / st_L[h0]);
   out[h1 * kHeadDim + d0] = f2bf(acc[1] / st_L[h1]);
   if (tid == 0) p.tickets[m * p.kv_heads + g] = 0u;
+  if (p.heads_done) {
+    // publish the (token, kv head)'s output to the CTAs that consume it in
+    // this launch (release after the barrier covers every thread's stores)
+    sync();
+    if (tid == 0) red_add_release_gpu(p.heads_done, 1u);
+  }
+  return tid == 0;
+}
+
+constexpr int kAttnStages = 3;
+constexpr int kAttnThreads = kAttnConsumers + 32;  // + one producer warp
+
+struct AttnSmem {
+  static constexpr size_t STAGE = size_t(kSub) * kHeadDim * 2;  // one of K or V
+  static constexpr size_t K_OFF = 0;
+  static constexpr size_t V_OFF = K_OFF + kAttnStages * STAGE;
+  static constexpr size_t BAR_OFF = V_OFF + kAttnStages * STAGE;   // full, empty
+  static constexpr size_t SCR_OFF = BAR_OFF + 2 * kAttnStages * 8;
+  static constexpr size_t BYTES = SCR_OFF + AttnScratch::BYTES;
+  static_assert(kAttnStages * STAGE >= size_t(kAttnWarps) * kGroup * kHeadDim * 4,
+                "the K ring stages the cross-warp combine");
+  static_assert(SCR_OFF % 16 == 0, "scratch alignment");
+};
+
+struct ConsumerSync {
+  __device__ void operator()() const { named_sync(1, kAttnConsumers); }
+};
+
+// One CTA of the split-KV attention, (split s, kv head g, token m): a
+// producer warp streams its positions in 64-position sub-chunks through a
+// 3-stage cp.async.bulk ring; rows of the history (< the step's first
+// position) are fetched before griddepcontrol.wait, rows written by this
+// step's QKV kernel after it. `cta` is the CTA's index in the launch trace.
+// Returns true in thread 0 of the CTA that merged the (token, kv head).
+static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, unsigned cta, uint8_t* smem) {
+  uint16_t* ks = reinterpret_cast<uint16_t*>(smem + AttnSmem::K_OFF);
+  uint16_t* vs = reinterpret_cast<uint16_t*>(smem + AttnSmem::V_OFF);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + AttnSmem::BAR_OFF);
+  uint64_t* empty = full + kAttnStages;
+  uint8_t* scratch = smem + AttnSmem::SCR_OFF;
+
+  const uint64_t t0 = trace_now(p.trace);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  int64_t pos0, start, stop;
+  const int nsub = attn_range(p, s, m, pos0, start, stop);
+
+  if (tid == 0) {
+    for (int i = 0; i < kAttnStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kAttnWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kAttnWarps) {
+    // ---------------- producer
+    if (lane == 0) {
+      bool waited = false;
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint16_t* kbase = p.k_cache + int64_t(g) * p.cache_len * kHeadDim;
+      const uint16_t* vbase = p.v_cache + int64_t(g) * p.cache_len * kHeadDim;
+      for (int i = 0; i < nsub; ++i) {
+        const int64_t t0 = start + int64_t(i) * kSub;
+        const int rows = int(min(int64_t(kSub), stop - t0));
+        if (!waited && t0 + kSub > pos0) {  // touches rows written by this step
+          grid_dep_wait();
+          waited = true;
+        }
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 202)) return false;
+        const uint32_t bytes = uint32_t(rows) * kHeadDim * 2;
+        mbar_arrive_expect_tx(&full[stage], 2 * bytes);
+        bulk_g2s(ks + size_t(stage) * kSub * kHeadDim, kbase + t0 * kHeadDim, bytes, &full[stage]);
+        bulk_g2s(vs + size_t(stage) * kSub * kHeadDim, vbase + t0 * kHeadDim, bytes, &full[stage]);
+        if (++stage == kAttnStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    return false;
+  }
+
+  // ---------------- consumers
+  // q comes from the QKV kernel. No early griddepcontrol.launch_dependents:
+  // the next kernel (o_proj) starts when this grid exits, since its CTAs
+  // would otherwise stream weights during this kernel's latency-bound
+  // publish/merge and slow it (decode step 3.37 -> 3.12 ms measured).
+  grid_dep_wait();
+  const uint64_t t1 = trace_now(p.trace);
+  uint64_t qd[kGroup][4];
+  attn_load_q(p, m, g, qd);
+  AttnWarpState ws;
+  attn_state_init(ws);
+  float* pw = reinterpret_cast<float*>(scratch + AttnScratch::PW) + warp * 80;
+  int stage = 0;
+  uint32_t phase = 0;
+  bool failed = false;  // a timed-out wait records the error; control flow is unchanged
+  for (int i = 0; i < nsub; ++i) {
+    const int64_t t0 = start + int64_t(i) * kSub;
+    const int rows = int(min(int64_t(kSub), stop - t0));
+    if (!failed && !mbar_wait(&full[stage], phase, p.err, 203)) failed = true;
+    attn_rows(ks + size_t(stage) * kSub * kHeadDim, vs + size_t(stage) * kSub * kHeadDim, rows, qd, ws, pw);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == kAttnStages) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+  const uint64_t t2 = trace_now(p.trace);
+  const bool merged = attn_publish(p, s, g, m, pos0, ws, scratch, reinterpret_cast<float*>(ks), ConsumerSync());
+  if (tid == 0) trace_commit(p.trace, p.trace_tag, cta, t0, t1, t2);
+  return merged;
 }
 
 }  // namespace cb
