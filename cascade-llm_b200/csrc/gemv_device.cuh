@@ -124,10 +124,9 @@ __device__ __forceinline__ float key_value(uint32_t key) {
 // Warp-cooperative top-k of entries [lo, hi) of `keys` (shared memory) with
 // distinct ids id_of(c): round r takes the largest key and, among equal
 // keys, the smallest id (two warp reductions), removes it from `keys` and
-// stages it at out_key[r] / out_id[r] (key 0 once the range is exhausted).
-template <class IdOf>
-__device__ __forceinline__ void warp_topk(uint32_t* keys, IdOf id_of, int lo, int hi, int k, uint32_t* out_key,
-                                          uint32_t* out_id) {
+// hands it to emit(r, key, id) in lane 0 (key 0 once the range is exhausted).
+template <class IdOf, class Emit>
+__device__ __forceinline__ void warp_topk(uint32_t* keys, IdOf id_of, int lo, int hi, int k, Emit emit) {
   const int lane = threadIdx.x & 31;
   for (int r = 0; r < k; ++r) {
     uint32_t bk = 0u, bi = 0xFFFFFFFFu;
@@ -145,10 +144,7 @@ __device__ __forceinline__ void warp_topk(uint32_t* keys, IdOf id_of, int lo, in
     const uint32_t wk = __reduce_max_sync(0xFFFFFFFFu, bk);
     const uint32_t wi = __reduce_min_sync(0xFFFFFFFFu, bk == wk ? bi : 0xFFFFFFFFu);
     if (wk != 0u && bk == wk && bi == wi) keys[bp] = 0u;  // exactly one lane owns it
-    if (lane == 0) {
-      out_key[r] = wk;
-      out_id[r] = wi;
-    }
+    if (lane == 0) emit(r, wk, wi);
     __syncwarp();
   }
 }
@@ -160,21 +156,22 @@ __device__ __forceinline__ void warp_topk(uint32_t* keys, IdOf id_of, int lo, in
 template <class IdOf>
 static __device__ void block_topk(uint32_t* keys, IdOf id_of, int n, int k, uint32_t* stage, float* out_v,
                                   int64_t* out_i) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   constexpr int W = kThreads / 32;
-  uint32_t* st_key = stage;
-  uint32_t* st_id = stage + W * k;
-  warp_topk(keys, id_of, int(int64_t(n) * warp / W), int(int64_t(n) * (warp + 1) / W), k, st_key + warp * k,
-            st_id + warp * k);
+  uint32_t* st_key = stage + warp * k;
+  uint32_t* st_id = stage + W * k + warp * k;
+  warp_topk(keys, id_of, int(int64_t(n) * warp / W), int(int64_t(n) * (warp + 1) / W), k,
+            [st_key, st_id](int r, uint32_t key, uint32_t id) {
+              st_key[r] = key;
+              st_id[r] = id;
+            });
   __syncthreads();
   if (warp != 0) return;
-  warp_topk(st_key, [st_id](int c) { return st_id[c]; }, 0, W * k, k, st_key, st_id);
-  __syncwarp();
-  for (int r = lane; r < k; r += 32) {
-    const uint32_t key = st_key[r];
+  const uint32_t* ids = stage + W * k;
+  warp_topk(stage, [ids](int c) { return ids[c]; }, 0, W * k, k, [out_v, out_i](int r, uint32_t key, uint32_t id) {
     out_v[r] = key ? key_value(key) : -__int_as_float(0x7F800000);
-    out_i[r] = key ? int64_t(st_id[r]) : INT64_MAX;
-  }
+    out_i[r] = key ? int64_t(id) : INT64_MAX;
+  });
 }
 
 // Reference selection over candidate lists in global memory by one warp,

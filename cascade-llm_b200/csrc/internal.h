@@ -50,6 +50,7 @@ int configure_smem(const char* what, void (*kernel)(KArgs...), size_t bytes) {
 
 int prepare_gemv();
 int prepare_attention();
+int prepare_attention_oproj();
 int prepare_gemm();
 int prepare_prefill_attention();
 

@@ -238,6 +238,7 @@ extern "C" int cb_sm_count(void) { return sm_count(); }
 extern "C" int cb_prepare(void) {
   int rc = prepare_gemv();
   if (rc == kOk) rc = prepare_attention();
+  if (rc == kOk) rc = prepare_attention_oproj();
   if (rc == kOk) rc = prepare_gemm();
   if (rc == kOk) rc = prepare_prefill_attention();
   return rc;

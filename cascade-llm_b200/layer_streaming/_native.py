@@ -76,6 +76,8 @@ _SIGNATURES = {
     "cb_attention_workspace_bytes": (_I64, [_I, _I]),
     "cb_attention": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "cb_attention_noalloc": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _P, _P]),
+    "cb_attention_oproj_max_splits": (_I, []),
+    "cb_attention_oproj": (_I, [_P, _P, _P, _I64, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
     "cb_memcpy_h2d_async": (_I, [_P, _P, _I64, _P]),
     "cb_host_gather_rows": (_I, [_P, _P, _I64, _I64, _P, _I64]),
     "cb_ring_create": (_I, [_I, _PP, _I64, _P, _PP, _I64, _I, _PP]),

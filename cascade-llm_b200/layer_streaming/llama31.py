@@ -90,6 +90,10 @@ def llama3_inv_freq(config):
     return torch.where(medium, smoothed, scaled)
 
 
+FUSED_ATTENTION_MAX_LENGTH = 8192  # one-token steps up to this context run attention + o_proj as one kernel
+FUSED_ATTENTION_SPLITS = 16        # KV splits per head of the fused kernel (128 CTAs; 168 stream W_o)
+
+
 def attention_split(tokens, length, sm_count, kv_heads=8):
     """(splits, chunk) for the split-KV attention kernel: about two CTAs per
     SM over (splits x KV heads x tokens), chunks a multiple of 64 positions."""
@@ -242,6 +246,8 @@ class Llama31DecodeExecutor:
             self._ids_dev = torch.zeros(1, dtype=torch.int64, device=self.device)  # one-token step input
         self._embed_pending = False
         self.sm_count = int(lib.cb_sm_count())
+        self.fuse_attention = os.environ.get("CASCADE_B200_FUSED_ATTENTION", "1") != "0"
+        self._fused_max_splits = int(lib.cb_attention_oproj_max_splits())
         self._graphs = {}
         self._rows = 0
         self._buffers(1)
@@ -262,12 +268,21 @@ class Llama31DecodeExecutor:
         self._q = torch.empty((rows, 4096), dtype=torch.bfloat16, device=dev)
         self._attn = torch.empty((rows, 4096), dtype=torch.bfloat16, device=dev)
         self._mlp = torch.empty((rows, 14336), dtype=torch.bfloat16, device=dev)
-        self._tickets = torch.zeros(8 * rows, dtype=torch.int32, device=dev)  # kept zero by the kernel
+        # per (token, KV head) tickets, then the fused kernel's two counters (kept zero by the kernels)
+        self._tickets = torch.zeros(8 * rows + 8, dtype=torch.int32, device=dev)
         self._rows = rows
         self._graphs.clear()
 
     def attention_config(self, tokens, length):
-        return attention_split(tokens, length, self.sm_count)
+        """(splits, chunk, fused) of the decode attention for `length` keys:
+        chunk 0 lets the kernel size the splits from the device position, so
+        one captured launch serves every length up to `length`; fused runs
+        attention and o_proj as one kernel (one-token steps)."""
+
+        if tokens == 1 and self.fuse_attention and length <= FUSED_ATTENTION_MAX_LENGTH:
+            return min(FUSED_ATTENTION_SPLITS, self._fused_max_splits), 0, True
+        splits, _ = attention_split(tokens, length, self.sm_count)
+        return splits, 0, False
 
     def _attention_workspace(self, tokens, splits):
         need = ops.attention_workspace_bytes(tokens, splits)
@@ -323,7 +338,7 @@ class Llama31DecodeExecutor:
             position_ids=torch.arange(past, past + tokens, dtype=torch.long).unsqueeze(0),
         )
 
-    def _unit(self, layer, operation, weights, splits=None, chunk=None):
+    def _unit(self, layer, operation, weights, splits=None, chunk=None, fused=None):
         tokens = self._tokens
         cache = self.kv_cache
         eps = self.eps
@@ -354,17 +369,19 @@ class Llama31DecodeExecutor:
                     kc if wk is not None else None, vc if wv is not None else None,
                 )
         elif operation == "o_proj":
+            wo = w("o_proj")
             if gemm:  # prefill: causal flash attention on the tensor cores
                 ops.prefill_attention(self._q[:tokens], kc, vc, pos, self._attn[:tokens])
-            else:
-                if splits is None:
-                    splits, chunk = self.attention_config(tokens, cache.length + tokens)
-                ws = self._attention_workspace(tokens, splits)
-                ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
-            wo = w("o_proj")
-            if gemm:
                 ops.gemm_residual(self._attn[:tokens], wo, self._x[:tokens], self._x[:tokens])
+                return
+            if splits is None:
+                splits, chunk, fused = self.attention_config(tokens, cache.length + tokens)
+            ws = self._attention_workspace(tokens, splits)
+            if fused:
+                ops.attention_oproj(self._q[0], kc, vc, pos, splits, wo, self._x[0], self._attn[0], self._x[0], ws,
+                                    self._tickets)
             else:
+                ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
                 ops.proj_residual(self._attn[0], wo, self._x[0], self._x[0])
         elif operation == "gate_up":
             wg, wu = w("gate_proj"), w("up_proj")
@@ -423,9 +440,9 @@ class Llama31DecodeExecutor:
         length = self.kv_cache.length + 1
         bucket = max(64, 1 << (length - 1).bit_length())
         bucket = min(bucket, self.kv_cache.capacity)
-        splits, chunk = self.attention_config(1, bucket)
+        splits, chunk, fused = self.attention_config(1, bucket)
         embed = self._embed_pending  # the graph starts with the embedding of the step's id
-        key = (id(runtime), bucket, self.kv_cache.generation, self._rows, embed)
+        key = (id(runtime), bucket, self.kv_cache.generation, self._rows, embed, fused)
         graph = self._graphs.get(key)
         if graph is None:
             self._attention_workspace(1, splits)
@@ -436,7 +453,7 @@ class Llama31DecodeExecutor:
                     self._embed_one()
                 for index, unit in enumerate(units):
                     for operation in _UNIT_OPS.get(unit.operation, (unit.operation,)):
-                        self._unit(unit.layer_index, operation, runtime.unit_views(index), splits, chunk)
+                        self._unit(unit.layer_index, operation, runtime.unit_views(index), splits, chunk, fused)
                 ops.position_advance(self.kv_cache.position, 1)
             self.kv_cache.length = saved
             self._graphs[key] = graph

@@ -44,6 +44,10 @@ _SCHEMAS = {
         "attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor position, int splits, int chunk, "
         "Tensor(a!) out, Tensor(b!) workspace, Tensor(c!) tickets) -> ()"
     ),
+    "attention_oproj": (
+        "attention_oproj(Tensor q, Tensor k_cache, Tensor v_cache, Tensor position, int splits, Tensor wo, "
+        "Tensor residual, Tensor(a!) attn_out, Tensor(b!) out, Tensor(c!) workspace, Tensor(d!) tickets) -> ()"
+    ),
     "position_set": "position_set(Tensor(a!) position, Tensor? src, int value) -> ()",
     "gemm_bf16": "gemm_bf16(Tensor a, Tensor w, Tensor(a!) out) -> ()",
     "prefill_attention": (
@@ -213,6 +217,28 @@ def attention(q, k_cache, v_cache, position, splits, chunk, out, workspace, tick
             nat.ptr(tickets, torch.int32, "tickets"), _stream(q),
         ),
         "cascade.attention",
+    )
+
+
+def attention_oproj_max_splits():
+    return int(nat.lib().cb_attention_oproj_max_splits())
+
+
+def attention_oproj(q, k_cache, v_cache, position, splits, wo, residual, attn_out, out, workspace, tickets):
+    """One-token attention (8 KV heads) fused with o_proj + residual add."""
+
+    if k_cache.shape[-3] != 8 or q.numel() != 4096 or wo.shape != (4096, 4096):
+        raise ValueError("attention_oproj is the one-token, 8-KV-head layout")
+    if tickets.numel() < 10:
+        raise ValueError("attention_oproj needs 10 zeroed tickets")
+    nat.check(
+        nat.lib().cb_attention_oproj(
+            nat.ptr(q, BF16, "q"), nat.ptr(k_cache, BF16, "k_cache"), nat.ptr(v_cache, BF16, "v_cache"),
+            k_cache.shape[-2], nat.ptr(position, torch.int32, "position"), int(splits), nat.ptr(wo, BF16, "wo"),
+            nat.ptr(residual, BF16, "residual"), nat.ptr(attn_out, BF16, "attn_out"), nat.ptr(out, BF16, "out"),
+            nat.ptr(workspace, None, "workspace"), nat.ptr(tickets, torch.int32, "tickets"), _stream(q),
+        ),
+        "cascade.attention_oproj",
     )
 
 

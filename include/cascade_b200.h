@@ -173,6 +173,24 @@ int cb_attention(const void* q, const void* k_cache, const void* v_cache, int64_
                  const int32_t* position, int M, int kv_heads, int splits, int chunk, void* out,
                  void* workspace, unsigned int* tickets, void* stream);
 
+/* One-token decode attention fused with the o_proj projection and its
+ * residual add: out = bf16(residual + bf16(attn . W_o^T)), attn the GQA
+ * attention of the token at *position over the cache [0, *position] (8 KV
+ * heads, written to attn_out [4096] as well). Replaces llama31.py:182-250
+ * (SDPA, o_proj F.linear, residual add) in one launch: the o_proj weights
+ * stream into registers and shared memory while the attention runs, and the
+ * projection finishes as soon as the 8 heads are merged. Bit-identical to
+ * cb_attention (chunk 0) followed by cb_proj_residual. splits: 1 ..
+ * cb_attention_oproj_max_splits() (16 fits a B200); chunks are sized on the
+ * device. wo: [4096, 4096]; residual/out: [4096] (may alias). workspace:
+ * cb_attention_workspace_bytes(1, splits) bytes; tickets: 10 uint32 zeroed
+ * once by the caller (left zero by each launch). Error code 205: the
+ * projection's wait for the attention gave up (2 s). */
+int cb_attention_oproj_max_splits(void);
+int cb_attention_oproj(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
+                       const int32_t* position, int splits, const void* wo, const void* residual, void* attn_out,
+                       void* out, void* workspace, unsigned int* tickets, void* stream);
+
 /* Allocation-free variant of cb_attention, for callers that cannot allocate
  * device memory (a host framework that owns the whole memory budget in its
  * own pool, or a latency-critical loop where cudaMalloc would synchronise the

@@ -346,3 +346,57 @@ def test_attention_with_too_few_splits_reports_code_204(ops, cuda):
         torch.testing.assert_close(out.float(), sdpa.float(), rtol=2e-2, atol=2e-2)
     finally:
         lib.cb_set_error_word(None)
+
+
+@pytest.mark.parametrize("length", [1, 37, 300, 2048, 5000, 8192])
+def test_adaptive_split_chunks(ops, cuda, length):
+    """chunk = 0: the kernel sizes the splits from the device position, so one
+    launch configuration serves every length (SDPA tolerance, tickets zero)."""
+
+    kc, vc, k, v = _cache_with_rope(length, length + 64, 70, cuda)
+    q = randn((1, 32, 1, 128), 71)
+    pos = torch.tensor([length - 1], dtype=torch.int32, device=cuda)
+    sdpa = lo.attention(q, k, v, causal=False).view(4096)
+    for splits in (1, 16, 37):
+        out = torch.empty(4096, dtype=BF16, device=cuda)
+        ws = torch.empty(ops.attention_workspace_bytes(1, splits), dtype=torch.uint8, device=cuda)
+        tickets = torch.zeros(8, dtype=torch.int32, device=cuda)
+        ops.attention(q.view(4096), kc, vc, pos, splits, 0, out, ws, tickets)
+        torch.testing.assert_close(out.float(), sdpa.float(), rtol=2e-2, atol=2e-2)
+        assert int(tickets.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("length", [1, 37, 300, 2048, 8192])
+def test_fused_attention_oproj_equals_separate_kernels(ops, cuda, length):
+    """cb_attention_oproj == cb_attention (chunk 0) + cb_proj_residual, bit
+    for bit, on two launches in a row (the counters return to zero)."""
+
+    from layer_streaming import _native
+
+    kc, vc, k, v = _cache_with_rope(length, length + 64, 80, cuda)
+    q = randn((1, 32, 1, 128), 81).view(4096)
+    wo = randn((4096, 4096), 82, 0.02)
+    x = randn((4096,), 83)
+    pos = torch.tensor([length - 1], dtype=torch.int32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    lib = _native.lib()
+    lib.cb_set_error_word(err.data_ptr())
+    try:
+        for splits in sorted({1, 8, 16, ops.attention_oproj_max_splits()}):
+            ws = torch.empty(ops.attention_workspace_bytes(1, splits), dtype=torch.uint8, device=cuda)
+            tickets = torch.zeros(16, dtype=torch.int32, device=cuda)
+            attn_ref = torch.empty(4096, dtype=BF16, device=cuda)
+            ops.attention(q, kc, vc, pos, splits, 0, attn_ref, ws, tickets)
+            want = torch.empty(4096, dtype=BF16, device=cuda)
+            ops.proj_residual(attn_ref, wo, x, want)
+            for _ in range(2):
+                attn = torch.empty(4096, dtype=BF16, device=cuda)
+                out = x.clone()
+                ops.attention_oproj(q, kc, vc, pos, splits, wo, out, attn, out, ws, tickets)
+                torch.cuda.synchronize()
+                assert torch.equal(attn, attn_ref), splits
+                assert torch.equal(out, want), splits
+                assert int(tickets.abs().sum()) == 0
+            assert int(err.item()) == 0
+    finally:
+        lib.cb_set_error_word(None)
