@@ -162,7 +162,8 @@ __device__ __forceinline__ uint32_t wait_tagged(const uint64_t* p, uint32_t tag,
 // word 0 is the record cursor, word 1 the capacity in records; record r
 // (8 words at 8 * (r + 1)) holds the launch tag << 32 | CTA index, the SM,
 // and %globaltimer at CTA start, after the dependency wait, after the main
-// loop and at the end. A null buffer (the default) records nothing.
+// loop and at the end, then two kernel-specific points (the LM head: its
+// CTA's top-k selected, its ticket taken). A null buffer records nothing.
 __device__ __forceinline__ uint32_t smid_u32() {
   uint32_t v;
   asm volatile("mov.u32 %0, %%smid;" : "=r"(v));
@@ -170,7 +171,7 @@ __device__ __forceinline__ uint32_t smid_u32() {
 }
 __device__ __forceinline__ uint64_t trace_now(const uint64_t* trace) { return trace ? globaltimer_ns() : 0; }
 __device__ __forceinline__ void trace_commit(uint64_t* trace, uint32_t tag, uint32_t cta, uint64_t t0, uint64_t t1,
-                                             uint64_t t2) {
+                                             uint64_t t2, uint64_t x0 = 0, uint64_t x1 = 0) {
   if (!trace) return;
   const uint64_t t3 = globaltimer_ns();
   const unsigned long long slot = atomicAdd(reinterpret_cast<unsigned long long*>(trace), 1ull);
@@ -182,6 +183,8 @@ __device__ __forceinline__ void trace_commit(uint64_t* trace, uint32_t tag, uint
   r[3] = t1;
   r[4] = t2;
   r[5] = t3;
+  r[6] = x0;  // kernel-specific extra points (0: none)
+  r[7] = x1;
 }
 
 // ------------------------------------------------------------ loads/stores

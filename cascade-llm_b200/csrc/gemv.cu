@@ -54,8 +54,11 @@ static int lm_head_grid() { return gemv_grid(); }
 template <int K>
 __global__ void __launch_bounds__(kThreads, CB_GEMV_CTAS_PER_SM) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t times[3];  // launch trace: start, after the wait, after the main loop
-  if (p.trace && threadIdx.x == 0) times[0] = globaltimer_ns();
+  __shared__ uint64_t times[5];  // launch trace: start, after the wait, after the main loop, two extra points
+  if (p.trace && threadIdx.x == 0) {
+    times[0] = globaltimer_ns();
+    times[3] = times[4] = 0;
+  }
   GemvRegs<K, CB_GEMV_DEPTH> r;
   gemv_prefetch<K, CB_GEMV_DEPTH>(p, blockIdx.x, gridDim.x, r);
   grid_dep_wait();  // the activation row comes from the previous kernel
@@ -64,7 +67,8 @@ __global__ void __launch_bounds__(kThreads, CB_GEMV_CTAS_PER_SM) gemv_kernel(con
     grid_dep_launch();
   }
   gemv_run<K, CB_GEMV_DEPTH>(p, smem, blockIdx.x, gridDim.x, r, p.trace ? &times[2] : nullptr);
-  if (p.trace && threadIdx.x == 0) trace_commit(p.trace, p.trace_tag, blockIdx.x, times[0], times[1], times[2]);
+  if (p.trace && threadIdx.x == 0)
+    trace_commit(p.trace, p.trace_tag, blockIdx.x, times[0], times[1], times[2], times[3], times[4]);
 }
 
 }  // namespace cb

@@ -611,10 +611,12 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   }
   __syncthreads();
   if (tid == 0) {
+    if (t_loop) t_loop[1] = trace_now(p.trace);
     // acq_rel: publishes this CTA's candidates (written before the barrier)
     // and, for the last CTA, orders its reads after everyone's
     const unsigned int ticket = atom_add_acq_rel_gpu(p.ticket, 1u);
     red[15] = __int_as_float(ticket == unsigned(ncta - 1) ? 1 : 0);
+    if (t_loop) t_loop[2] = trace_now(p.trace);
   }
   __syncthreads();
   if (__float_as_int(red[15]) != 1) return;
