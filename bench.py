@@ -87,6 +87,7 @@ def parse_args():
                         help="BASELINE config 3: each projection at M in {1, 6, 64, 512}, HBM-resident and "
                              "H2D-streamed through two slots (one JSON line per case)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-streamed", action="store_true", help="skip the H2D-streamed mode measurement")
     parser.add_argument("--profile-range", action="store_true",
                         help="after warm-up, run --steps decode steps between cudaProfilerStart/Stop "
                              "(for `ncu --profile-from-start off`) and exit")
@@ -668,6 +669,41 @@ def reference_arm(args, rank):
     }
 
 
+def tp_streamed(args, world, rank, device, barrier, steps=3):
+    """The reference's H2D-streamed mode under tensor parallelism: every rank
+    streams only its layer shards (13.96 GB / N per token) from its own pinned
+    shard arena through two device slots; a short prompt, then timed decode
+    steps (max over ranks)."""
+
+    import torch.distributed as dist
+
+    from layer_streaming.tensor_parallel import TensorParallelDecoder, TensorParallelWeights
+
+    weights = TensorParallelWeights.seeded(world, rank, device, seed=0, stream_layers=True)
+    decoder = TensorParallelDecoder(Config(), weights, top_k=10, max_length=256, profile=True)
+    with torch.inference_mode():
+        token = decoder(random_ids(64, seed=1).to(device)).topk_indices[..., 0].reshape(1, 1)
+        token = decoder(token).topk_indices[..., 0].reshape(1, 1)  # warm-up
+        torch.cuda.synchronize()
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            token = decoder(token).topk_indices[..., 0].reshape(1, 1)
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    prof = decoder.last_stream
+    gbps = prof["h2d_bytes"] / 1e9 / (prof["h2d_event_sum_ms"] / 1000.0)
+    t = torch.tensor([start.elapsed_time(end) / steps, -gbps], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    decoder.close()
+    return {"ms_per_token": round(float(t[0]), 2), "steps": steps,
+            "h2d_bytes_per_token_per_rank": int(prof["h2d_bytes"]),
+            "h2d_gbps_per_rank_min": round(-float(t[1]), 2),
+            "note": "stream_layers shards: each rank streams its own 1/N of the layer weights (PCIe-bound)"}
+
+
 def tensor_parallel(args, world, rank, local, device):
     """N>1: one request decoded by all ranks (tensor parallelism over heads,
     FFN rows and vocabulary), strong scaling of the same workload."""
@@ -762,6 +798,7 @@ def tensor_parallel(args, world, rank, local, device):
     end.synchronize()
     gate_up_ms = start.elapsed_time(end) / (4 * len(mats))
     gate_up_bytes = GATE_UP_BYTES // world
+    streamed = None if args.no_streamed else tp_streamed(args, world, rank, device, barrier)
     peak, peak_kind = measured_peak()
     achieved = gate_up_bytes / (gate_up_ms / 1000.0) / 1e9
     context = decoder.kv_cache.length - args.steps - 1
@@ -797,6 +834,7 @@ def tensor_parallel(args, world, rank, local, device):
             "frac": round(rank_gbs / peak, 4), "bytes_per_token_per_rank": rank_bytes,
         },
         "cpu_baseline": None,
+        "streamed_mode": streamed,
         "prefill": {"tokens": args.context, "chunk": 512, "ms": round(prefill_ms, 2),
                     "tokens_per_s": round(args.context / (prefill_ms / 1000.0), 1)},
         "gpu_launches": (1 + 32 * 5 + 1 + 2) * args.steps if args.exchange == "peer" else None,
@@ -856,7 +894,7 @@ def main():
     executor.check_errors()
     e2e = time_e2e(executor, runtime, token, args.steps)
     gate_up_ms = time_gate_up(executor, runtime, plan)
-    streamed = time_streamed(plan, store, resident, executor, device, token)
+    streamed = None if args.no_streamed else time_streamed(plan, store, resident, executor, device, token)
     peak, peak_kind = measured_peak()
     context = executor.kv_cache.length - args.steps - 1  # mean cached length over the timed steps
     achieved = GATE_UP_BYTES / (gate_up_ms / 1000.0) / 1e9

@@ -48,14 +48,16 @@ struct AttnScratch {
 };
 
 // Positions per split: p.chunk, or (p.chunk == 0) sized on the device from
-// the step's position so that the splits cover the longest context of the
-// step in whole 64-position sub-chunks (every split holds keys once the
-// context has splits x 64 positions).
+// the step's position: the least multiple of 64 positions, and at least
+// kMinChunk, with which the launch's splits cover the longest context of the
+// step. Short contexts leave the last splits empty rather than give every
+// CTA a single sub-chunk (more partials to merge for the same bytes).
+constexpr int64_t kMinChunk = 2 * kSub;
 __device__ __forceinline__ int64_t attn_chunk(const AttnParams& p, int64_t pos0) {
   if (p.chunk > 0) return p.chunk;
   const int64_t longest = min(pos0 + p.M, p.cache_len);
   const int64_t per = (longest + p.splits - 1) / p.splits;
-  return max(int64_t(kSub), (per + kSub - 1) / kSub * kSub);
+  return max(kMinChunk, (per + kSub - 1) / kSub * kSub);
 }
 
 // Positions [start, stop) of split s for token m, and the sub-chunk count.

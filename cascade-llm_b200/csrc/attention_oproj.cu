@@ -111,13 +111,17 @@ static __device__ void oproj_cta(const AttnOprojParams& p, int cta, int ncta, ui
   if (tid == 0) {
     const uint64_t began = globaltimer_ns();
     bool ok = false;
+    // relaxed polls with a short back-off (one thread per CTA), then one
+    // acquire fence: the attention's output stores are visible after it
     for (uint32_t i = 0; i < (kSpinLimit << 4); ++i) {
-      if (ld_acquire_gpu(p.counters) >= 8u) {
+      if (ld_relaxed_gpu(p.counters) >= 8u) {
         ok = true;
         break;
       }
-      if ((i & 255u) == 255u && globaltimer_ns() - began > p.wait_ns) break;
+      __nanosleep(100);
+      if ((i & 15u) == 15u && globaltimer_ns() - began > p.wait_ns) break;
     }
+    fence_acq_rel_gpu();
     if (!ok && p.err) atomicExch(p.err, 205);
     // every o_proj CTA is past the wait once the last one counts itself:
     // that one returns both counters to zero for the next launch

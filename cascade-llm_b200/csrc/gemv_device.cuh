@@ -149,6 +149,38 @@ __device__ __forceinline__ void warp_topk(uint32_t* keys, IdOf id_of, int lo, in
   }
 }
 
+// Register form of warp_topk for ranges of at most 32 * NPL entries: each
+// lane holds its (at most NPL) entries in registers, so a round is a local
+// selection, two warp reductions and one predicated removal - no shared
+// memory traffic between rounds.
+template <int NPL, class IdOf, class Emit>
+__device__ __forceinline__ void warp_topk_regs(const uint32_t* keys, IdOf id_of, int lo, int hi, int k, Emit emit) {
+  const int lane = threadIdx.x & 31;
+  uint32_t kk[NPL], ii[NPL];
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) {
+    const int c = lo + lane + 32 * j;
+    kk[j] = c < hi ? keys[c] : 0u;
+    ii[j] = c < hi ? id_of(c) : 0xFFFFFFFFu;
+  }
+  for (int r = 0; r < k; ++r) {
+    uint32_t bk = 0u, bi = 0xFFFFFFFFu;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      if (kk[j] > bk || (kk[j] == bk && kk[j] != 0u && ii[j] < bi)) {
+        bk = kk[j];
+        bi = ii[j];
+      }
+    }
+    const uint32_t wk = __reduce_max_sync(0xFFFFFFFFu, bk);
+    const uint32_t wi = __reduce_min_sync(0xFFFFFFFFu, bk == wk ? bi : 0xFFFFFFFFu);
+#pragma unroll
+    for (int j = 0; j < NPL; ++j)
+      if (wk != 0u && kk[j] == wk && ii[j] == wi) kk[j] = 0u;  // ids are distinct: one entry
+    if (lane == 0) emit(r, wk, wi);
+  }
+}
+
 // Exact top-k of n entries (keys in shared memory, ids by id_of) by the whole
 // CTA: each of the 8 warps selects the top-k of its eighth into `stage`
 // (8k keys, then 8k ids), then warp 0 selects the k best of those and writes
@@ -160,18 +192,27 @@ static __device__ void block_topk(uint32_t* keys, IdOf id_of, int n, int k, uint
   constexpr int W = kThreads / 32;
   uint32_t* st_key = stage + warp * k;
   uint32_t* st_id = stage + W * k + warp * k;
-  warp_topk(keys, id_of, int(int64_t(n) * warp / W), int(int64_t(n) * (warp + 1) / W), k,
-            [st_key, st_id](int r, uint32_t key, uint32_t id) {
-              st_key[r] = key;
-              st_id[r] = id;
-            });
+  auto to_stage = [st_key, st_id](int r, uint32_t key, uint32_t id) {
+    st_key[r] = key;
+    st_id[r] = id;
+  };
+  const int lo = int(int64_t(n) * warp / W), hi = int(int64_t(n) * (warp + 1) / W);
+  if (hi - lo <= 128)
+    warp_topk_regs<4>(keys, id_of, lo, hi, k, to_stage);
+  else
+    warp_topk(keys, id_of, lo, hi, k, to_stage);
   __syncthreads();
   if (warp != 0) return;
   const uint32_t* ids = stage + W * k;
-  warp_topk(stage, [ids](int c) { return ids[c]; }, 0, W * k, k, [out_v, out_i](int r, uint32_t key, uint32_t id) {
+  auto to_out = [out_v, out_i](int r, uint32_t key, uint32_t id) {
     out_v[r] = key ? key_value(key) : -__int_as_float(0x7F800000);
     out_i[r] = key ? int64_t(id) : INT64_MAX;
-  });
+  };
+  auto stage_id = [ids](int c) { return ids[c]; };
+  if (W * k <= 128)
+    warp_topk_regs<4>(stage, stage_id, 0, W * k, k, to_out);
+  else
+    warp_topk(stage, stage_id, 0, W * k, k, to_out);
 }
 
 // Reference selection over candidate lists in global memory by one warp,
@@ -240,14 +281,27 @@ static __device__ void block_merge_topk(const float* vals, const int64_t* idx, i
   uint32_t* ids = scratch + kMergeCap;
   uint32_t* stage = scratch + 2 * kMergeCap;
   const int n = G * k;
-  for (int c = tid; c < n; c += blockDim.x) {
-    const uint32_t key = order_key(__ldcg(vals + c));
-    const int64_t i = __ldcg(reinterpret_cast<const long long*>(idx) + c);
-    if (key >= thr && i != INT64_MAX) {
-      const int slot = atomicAdd(count, 1);
-      if (slot < kMergeCap) {
-        keys[slot] = key;
-        ids[slot] = uint32_t(i);
+  // eight candidates per thread in flight at a time (one L2 round trip per
+  // group instead of one per candidate)
+  constexpr int B = 8;
+  for (int base = tid; base < n; base += B * int(blockDim.x)) {
+    float v[B];
+    long long ix[B];
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      const int c = base + j * int(blockDim.x);
+      v[j] = c < n ? __ldcg(vals + c) : -__int_as_float(0x7F800000);
+      ix[j] = c < n ? __ldcg(reinterpret_cast<const long long*>(idx) + c) : INT64_MAX;
+    }
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      const uint32_t key = order_key(v[j]);
+      if (key >= thr && ix[j] != INT64_MAX) {
+        const int slot = atomicAdd(count, 1);
+        if (slot < kMergeCap) {
+          keys[slot] = key;
+          ids[slot] = uint32_t(ix[j]);
+        }
       }
     }
   }
@@ -437,6 +491,28 @@ __device__ __forceinline__ void gemv_load_batch(const GemvParams& p, int ub, int
   }
 }
 
+// Half `half` (registers [half * UB/2, (half + 1) * UB/2)) of the batch whose
+// first unit is ub.
+template <int K, int DEPTH = 1>
+__device__ __forceinline__ void gemv_load_half(const GemvParams& p, int ub, int u1, GemvRegs<K, DEPTH>& r, int half) {
+  using S = GemvShape<K, DEPTH>;
+  constexpr int H = S::UB / 2;
+  const int ul = S::ulane(threadIdx.x >> 5);
+#pragma unroll
+  for (int i = 0; i < S::UB; ++i) {
+    const int u = ub + i * S::UL + ul;
+    if ((i >= half * H && i < (half + 1) * H) && u < u1) {
+      const uint16_t *ra, *rb;
+      gemv_rows<K, DEPTH>(p, u, ra, rb);
+#pragma unroll
+      for (int c = 0; c < S::CPL; ++c) {
+        r.w[i][0][c] = ld_stream(ra + c * 256);
+        r.w[i][1][c] = ld_stream(rb + c * 256);
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void gemv_cta_units(const GemvParams& p, int cta, int ncta, int& u0, int& u1) {
   u0 = int(int64_t(p.total_units) * cta / ncta);
   u1 = int(int64_t(p.total_units) * (cta + 1) / ncta);
@@ -541,11 +617,12 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   }
 
   // dot products of one batch held in registers
-  auto consume = [&](const GemvRegs<K, DEPTH>& rr, int ub) {
+  // dot products of registers [i0, i1) of the batch whose first unit is ub
+  auto consume = [&](const GemvRegs<K, DEPTH>& rr, int ub, int i0, int i1) {
 #pragma unroll
     for (int i = 0; i < S::UB; ++i) {
       const int u = ub + i * S::UL + ul;
-      if (u < u1) {
+      if (i >= i0 && i < i1 && u < u1) {
         float a = 0.f, b = 0.f;
 #pragma unroll
         for (int c = 0; c < S::CPL; ++c) {
@@ -562,9 +639,24 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
       }
     }
   };
-  for (int ub = u0; ub < u1; ub += S::UB * S::UL) {
-    if (ub != u0) gemv_load_batch<K, DEPTH>(p, ub, u1, r);
-    consume(r, ub);
+  constexpr int STEP = S::UB * S::UL;  // units per batch of the CTA
+  if constexpr (S::UB % 2 == 0) {
+    // Two half-batches in flight: the registers of a batch are two halves,
+    // and as soon as one half is consumed the loads of the half one batch
+    // ahead go into it, so each lane keeps loads outstanding instead of
+    // waiting for a whole batch after consuming the previous one.
+    constexpr int H = S::UB / 2;
+    for (int ub = u0; ub < u1; ub += STEP) {
+      consume(r, ub, 0, H);
+      if (ub + STEP < u1) gemv_load_half<K, DEPTH>(p, ub + STEP, u1, r, 0);
+      consume(r, ub, H, S::UB);
+      if (ub + STEP < u1) gemv_load_half<K, DEPTH>(p, ub + STEP, u1, r, 1);
+    }
+  } else {
+    for (int ub = u0; ub < u1; ub += STEP) {
+      if (ub != u0) gemv_load_batch<K, DEPTH>(p, ub, u1, r);
+      consume(r, ub, 0, S::UB);
+    }
   }
   __syncthreads();
   if (t_loop && tid == 0) *t_loop = trace_now(p.trace);

@@ -90,8 +90,8 @@ def llama3_inv_freq(config):
     return torch.where(medium, smoothed, scaled)
 
 
-FUSED_ATTENTION_MAX_LENGTH = 8192  # one-token steps up to this context run attention + o_proj as one kernel
-FUSED_ATTENTION_SPLITS = 16        # KV splits per head of the fused kernel (128 CTAs; 168 stream W_o)
+FUSED_ATTENTION_MAX_LENGTH = 8192  # CASCADE_B200_FUSED_ATTENTION=1: one-token steps up to this context
+FUSED_ATTENTION_SPLITS = 18        # run attention + o_proj as one kernel (144 attention CTAs, 152 for W_o)
 
 
 def attention_split(tokens, length, sm_count, kv_heads=8):
@@ -246,7 +246,7 @@ class Llama31DecodeExecutor:
             self._ids_dev = torch.zeros(1, dtype=torch.int64, device=self.device)  # one-token step input
         self._embed_pending = False
         self.sm_count = int(lib.cb_sm_count())
-        self.fuse_attention = os.environ.get("CASCADE_B200_FUSED_ATTENTION", "1") != "0"
+        self.fuse_attention = os.environ.get("CASCADE_B200_FUSED_ATTENTION", "0") == "1"
         self._fused_max_splits = int(lib.cb_attention_oproj_max_splits())
         self._graphs = {}
         self._rows = 0

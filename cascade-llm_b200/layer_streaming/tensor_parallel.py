@@ -11,7 +11,9 @@ per GPU (``torchrun``), with the Megatron split of a Llama block:
   ``[128256r/N, 128256(r+1)/N)`` of the LM head; the embedding table, the
   norms and the residual stream are replicated;
 * attention, the QKV / gate-up projections and the LM head run on local
-  shards with no communication; o_proj and down_proj produce fp32 partial
+  shards with no communication (with ``stream_layers`` weights each rank
+  streams only its own layer shards from a pinned host arena through two
+  device slots every step, the reference's H2D mode split N ways); o_proj and down_proj produce fp32 partial
   sums that are all-reduced before the residual add (two exchanges per
   layer), and the LM head's per-rank top-k candidates are all-gathered and
   merged (one exchange per token).
@@ -124,15 +126,81 @@ def full_shape(key):
     raise KeyError(key)
 
 
-class TensorParallelWeights:
-    """This rank's weight shards, resident in HBM (bf16)."""
+# the transfer units of a rank's streamed layer shards, in stream order per
+# layer: (unit, [(matrix, rows, columns) of this rank's shard ...]); a unit's
+# pieces are consecutive rows of one contiguous block
+def shard_units(world):
+    q, kv, f = HEADS * HEAD_DIM // world, KV_HEADS * HEAD_DIM // world, FFN // world
+    return (
+        ("qkv", (("q_proj", q, HIDDEN), ("k_proj", kv, HIDDEN), ("v_proj", kv, HIDDEN))),
+        ("o_proj", (("o_proj", HIDDEN, HIDDEN // world),)),
+        ("gate_up", (("gate_proj", f, HIDDEN), ("up_proj", f, HIDDEN))),
+        ("down_proj", (("down_proj", HIDDEN, f),)),
+    )
 
-    def __init__(self, world, rank, device, tensors):
+
+class ShardArena:
+    """A rank's layer shards packed for H2D streaming: the 4 units of every
+    layer back to back (each unit 256-byte aligned) in ONE host arena
+    (pinned by default), so the rank streams only its own shard - 1/N of the
+    reference's per-token transfer (weight_store.py:184-206 streams the
+    whole model) - through the same two-slot pipeline."""
+
+    ALIGN = 128  # elements (256 bytes)
+
+    def __init__(self, world, rank, layers=LAYERS, pin=True):
+        _check_world(world, rank)
+        self.world = world
+        self.rank = rank
+        self.layers = layers
+        self.units = []  # (layer, unit name, element offset, elements, ((key, offset, rows, cols), ...))
+        cursor = 0
+        for layer in range(layers):
+            for name, pieces in shard_units(world):
+                placed, inner = [], 0
+                for matrix, rows, cols in pieces:
+                    placed.append((_matrix_key(layer, matrix), inner, rows, cols))
+                    inner += rows * cols
+                self.units.append((layer, name, cursor, inner, tuple(placed)))
+                cursor += -(-inner // self.ALIGN) * self.ALIGN
+        self.elements = cursor
+        self.unit_elements = max(u[3] for u in self.units)
+        self.storage = torch.empty(cursor, dtype=torch.bfloat16, pin_memory=pin)
+
+    @property
+    def nbytes(self):
+        return 2 * self.elements
+
+    def host_view(self, key):
+        for _, _, offset, _, pieces in self.units:
+            for k, inner, rows, cols in pieces:
+                if k == key:
+                    return self.storage.narrow(0, offset + inner, rows * cols).view(rows, cols)
+        raise KeyError(key)
+
+    def spans(self):
+        base = self.storage.data_ptr()
+        return [(base + 2 * offset, 2 * elements) for _, _, offset, elements, _ in self.units]
+
+    def views(self, index, slot):
+        """{key: device view} of unit ``index`` landed in ``slot``."""
+
+        return {k: slot.narrow(0, inner, rows * cols).view(rows, cols)
+                for k, inner, rows, cols in self.units[index][4]}
+
+
+class TensorParallelWeights:
+    """This rank's weight shards: resident in HBM (bf16), or with the layer
+    matrices in a :class:`ShardArena` streamed every step (``arena``) and
+    only the embedding, the norms and the LM-head shard resident."""
+
+    def __init__(self, world, rank, device, tensors, arena=None):
         _check_world(world, rank)
         self.world = world
         self.rank = rank
         self.device = torch.device(device)
         self.tensors = tensors
+        self.arena = arena
 
     def __getitem__(self, key):
         return self.tensors[key]
@@ -141,31 +209,47 @@ class TensorParallelWeights:
         return key in self.tensors
 
     @property
+    def streamed(self):
+        return self.arena is not None
+
+    @property
     def nbytes(self):
         return sum(t.numel() * t.element_size() for t in self.tensors.values())
 
+    @staticmethod
+    def _is_layer_matrix(key):
+        return key.startswith("model.layers.") and not key.endswith("layernorm.weight")
+
     @classmethod
-    def from_store(cls, store, world, rank, device):
-        """Shards of a loaded weight store (host arena, ``store.tensor(key)``)."""
+    def from_store(cls, store, world, rank, device, stream_layers=False):
+        """Shards of a loaded weight store (host arena, ``store.tensor(key)``);
+        ``stream_layers`` packs the layer matrices into a pinned
+        :class:`ShardArena` instead of HBM."""
 
         device = torch.device(device)
+        arena = ShardArena(world, rank) if stream_layers else None
         tensors = {}
         with torch.cuda.device(device):
             for key in model_keys():
                 part = shard_tensor(store.tensor(key), key, world, rank)
-                tensors[key] = part.to(device=device, non_blocking=False)
-        return cls(world, rank, device, tensors)
+                if arena is not None and cls._is_layer_matrix(key):
+                    arena.host_view(key).copy_(part)
+                else:
+                    tensors[key] = part.to(device=device, non_blocking=False)
+        return cls(world, rank, device, tensors, arena)
 
     @classmethod
-    def seeded(cls, world, rank, device, seed=0, std=0.02):
+    def seeded(cls, world, rank, device, seed=0, std=0.02, stream_layers=False):
         """The seeded random-init model of ``BaseWeightStore.fill_seeded``
         (element i of ``key`` = element i of stream ``cb_stream_key(seed,
         key)``; norms = 1), generated on the GPU and sharded: every rank's
-        shards are slices of the same full tensors."""
+        shards are slices of the same full tensors. ``stream_layers`` keeps
+        the layer matrices in a pinned :class:`ShardArena` (streamed mode)."""
 
         from .weight_store import is_norm
 
         device = torch.device(device)
+        arena = ShardArena(world, rank) if stream_layers else None
         tensors = {}
         with torch.cuda.device(device), torch.inference_mode():
             scratch = torch.empty(VOCAB * HIDDEN, dtype=torch.bfloat16, device=device)
@@ -179,10 +263,13 @@ class TensorParallelWeights:
                     full.fill_(1.0)
                 else:
                     ops.fill_normal_(full, _native.stream_key(seed, key), std=std)
-                tensors[key] = shard_tensor(full, key, world, rank).clone()
+                if arena is not None and cls._is_layer_matrix(key):
+                    arena.host_view(key).copy_(shard_tensor(full, key, world, rank))
+                else:
+                    tensors[key] = shard_tensor(full, key, world, rank).clone()
             del scratch
             torch.cuda.synchronize(device)
-        return cls(world, rank, device, tensors)
+        return cls(world, rank, device, tensors, arena)
 
 
 @dataclass
@@ -277,7 +364,7 @@ class TensorParallelDecoder:
     """
 
     def __init__(self, config, weights, group=None, top_k=10, max_length=None, use_graphs=True,
-                 exchange="peer"):
+                 exchange="peer", profile=False):
         for name, value in (("hidden_size", HIDDEN), ("intermediate_size", FFN),
                             ("num_hidden_layers", LAYERS), ("num_attention_heads", HEADS),
                             ("num_key_value_heads", KV_HEADS), ("vocab_size", VOCAB)):
@@ -305,7 +392,10 @@ class TensorParallelDecoder:
         self.ffn = FFN // world
         self.vocab_rows = VOCAB // world
         self.eps = float(getattr(config, "rms_norm_eps", 1e-5))
-        self.use_graphs = bool(use_graphs) and exchange == "peer"
+        # a streamed step waits on the host for its copies: it runs eagerly
+        self.use_graphs = bool(use_graphs) and exchange == "peer" and not weights.streamed
+        self.profile = bool(profile)
+        self.last_stream = None
         lib = _native.lib()
         with torch.cuda.device(self.device):
             _native.check(lib.cb_prepare(), "cb_prepare")
@@ -322,6 +412,16 @@ class TensorParallelDecoder:
             self.indices = torch.empty((1, 1, self.top_k), dtype=torch.int64, device=self.device)
             self._ids_dev = torch.zeros(1, dtype=torch.int64, device=self.device)  # one-token step input
         self.exchange_buffers = ExchangeBuffers(self.group, self.device) if exchange == "peer" else None
+        self._ring = None
+        if weights.streamed:
+            # two device slots of the largest unit, fed from this rank's pinned shard arena
+            from .streaming import SlotRing
+
+            self.slots = [torch.empty(weights.arena.unit_elements, dtype=torch.bfloat16, device=self.device)
+                          for _ in range(2)]
+            self.copy_stream = torch.cuda.Stream(device=self.device)
+            self.compute_stream = torch.cuda.Stream(device=self.device)
+            self._ring = SlotRing(self.slots, self.copy_stream)
         self.sm_count = int(lib.cb_sm_count())
         self._graphs = {}
         self._rows = 0
@@ -366,6 +466,9 @@ class TensorParallelDecoder:
 
     def close(self):
         self._graphs.clear()
+        if self._ring is not None:
+            self._ring.close()
+            self._ring = None
         if self.exchange_buffers is not None:
             self.exchange_buffers.close()
             self.exchange_buffers = None
@@ -399,36 +502,45 @@ class TensorParallelDecoder:
         self.group.all_reduce(self._partial[:tokens])
         ops.residual_add_f32(self._x[:tokens], self._partial[:tokens], self._x[:tokens])
 
-    def _layer(self, layer, tokens, splits, chunk, fused):
+    def _unit(self, layer, unit, mats, tokens, splits, chunk, fused):
+        """One transfer unit of a layer (``qkv``, ``o_proj``, ``gate_up`` or
+        ``down_proj``) with its weight matrices ``mats`` (resident shards, or
+        views of a device slot in the streamed mode)."""
+
         w = self.weights
         cache = self.kv_cache
         pos = cache.position
         kc, vc = cache.key(layer), cache.value(layer)
-        norm_in = w["model.layers.{}.input_layernorm.weight".format(layer)]
-        norm_post = w["model.layers.{}.post_attention_layernorm.weight".format(layer)]
-        if tokens > 1:  # prefill: tcgen05 GEMM over the step's tokens
-            ops.rmsnorm(self._x[:tokens], norm_in, self.eps, self._xn[:tokens])
-            ops.prefill_qkv_rope(self._xn[:tokens], self._w(layer, "q_proj"), self._w(layer, "k_proj"),
-                                 self._w(layer, "v_proj"), self.inv_freq, pos, self._q[:tokens], kc, vc,
-                                 self.q_heads, self.kv_heads)
+        m = lambda name: mats[_matrix_key(layer, name)]
+        if unit == "qkv":
+            norm_in = w["model.layers.{}.input_layernorm.weight".format(layer)]
+            if tokens > 1:  # prefill: tcgen05 GEMM over the step's tokens
+                ops.rmsnorm(self._x[:tokens], norm_in, self.eps, self._xn[:tokens])
+                ops.prefill_qkv_rope(self._xn[:tokens], m("q_proj"), m("k_proj"), m("v_proj"), self.inv_freq, pos,
+                                     self._q[:tokens], kc, vc, self.q_heads, self.kv_heads)
+            else:
+                ops.qkv_rope(self._x[0], norm_in, self.eps, m("q_proj"), m("k_proj"), m("v_proj"), self.inv_freq,
+                             pos, 0, self._q[0], kc, vc, self.q_heads, self.kv_heads)
+        elif unit == "o_proj":
+            if tokens > 1:
+                ops.prefill_attention(self._q[:tokens], kc, vc, pos, self._attn[:tokens])
+            else:
+                ws = self._attention_workspace(tokens, splits)
+                ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
+            self._proj(layer, 0, self._attn, m("o_proj"), tokens, fused)
+        elif unit == "gate_up":
+            norm_post = w["model.layers.{}.post_attention_layernorm.weight".format(layer)]
+            if tokens > 1:
+                ops.rmsnorm(self._x[:tokens], norm_post, self.eps, self._xn[:tokens])
+                ops.gemm_swiglu(self._xn[:tokens], m("gate_proj"), m("up_proj"), self._mlp[:tokens])
+            else:
+                ops.gate_up_swiglu(self._x[0], norm_post, self.eps, m("gate_proj"), m("up_proj"), self._mlp[0])
         else:
-            ops.qkv_rope(self._x[0], norm_in, self.eps, self._w(layer, "q_proj"), self._w(layer, "k_proj"),
-                         self._w(layer, "v_proj"), self.inv_freq, pos, 0, self._q[0], kc, vc,
-                         self.q_heads, self.kv_heads)
-        if tokens > 1:
-            ops.prefill_attention(self._q[:tokens], kc, vc, pos, self._attn[:tokens])
-        else:
-            ws = self._attention_workspace(tokens, splits)
-            ops.attention(self._q[:tokens], kc, vc, pos, splits, chunk, self._attn[:tokens], ws, self._tickets)
-        self._proj(layer, 0, self._attn, self._w(layer, "o_proj"), tokens, fused)
-        if tokens > 1:
-            ops.rmsnorm(self._x[:tokens], norm_post, self.eps, self._xn[:tokens])
-            ops.gemm_swiglu(self._xn[:tokens], self._w(layer, "gate_proj"), self._w(layer, "up_proj"),
-                            self._mlp[:tokens])
-        else:
-            ops.gate_up_swiglu(self._x[0], norm_post, self.eps, self._w(layer, "gate_proj"),
-                               self._w(layer, "up_proj"), self._mlp[0])
-        self._proj(layer, 1, self._mlp, self._w(layer, "down_proj"), tokens, fused)
+            self._proj(layer, 1, self._mlp, m("down_proj"), tokens, fused)
+
+    def _layer(self, layer, tokens, splits, chunk, fused):
+        for unit, _ in shard_units(self.group.world):
+            self._unit(layer, unit, self.weights, tokens, splits, chunk, fused)
 
     def _head(self, tokens):
         last = self._x[tokens - 1]
@@ -456,8 +568,18 @@ class TensorParallelDecoder:
 
     def _step(self, tokens, splits, chunk):
         fused = self.exchange == "peer" and tokens == 1
-        for layer in range(LAYERS):
-            self._layer(layer, tokens, splits, chunk, fused)
+        if self.weights.streamed:
+            arena = self.weights.arena
+
+            def body(index, slot):
+                layer, unit = arena.units[index][0], arena.units[index][1]
+                self._unit(layer, unit, arena.views(index, slot), tokens, splits, chunk, fused)
+
+            self.last_stream = self._ring.run(arena.spans(), body, self.compute_stream,
+                                              torch.cuda.current_stream(self.device), profile=self.profile)
+        else:
+            for layer in range(LAYERS):
+                self._layer(layer, tokens, splits, chunk, fused)
         self._head(tokens)
         ops.position_advance(self.kv_cache.position, tokens)
         ops.position_advance(self.epoch, 1)

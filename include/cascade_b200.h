@@ -162,9 +162,9 @@ int cb_topk_merge(const float* a_values, const int64_t* a_indices, int na, const
  * longest context of the step (the position lives on the device, so a launch
  * whose splits fall short records code 204 in the error word; the positions
  * beyond splits*chunk are then left out). chunk = 0: the kernel sizes the
- * chunks from the device position (the least multiple of 64 with which
- * `splits` chunks cover the step), so one captured launch serves every
- * context length and every split holds keys. workspace: cb_attention_workspace_bytes(M,
+ * chunks from the device position (the least multiple of 64, at least 128,
+ * with which `splits` chunks cover the step), so one captured launch serves
+ * every context length up to splits x chunk. workspace: cb_attention_workspace_bytes(M,
  * splits) bytes of scratch for the per-split partials (no initialisation).
  * tickets: M*kv_heads uint32 counters, zeroed once by the caller; each launch
  * leaves them zero. */

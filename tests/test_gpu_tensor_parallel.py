@@ -300,6 +300,35 @@ def test_world_of_one_decoder_reproduces_golden_run(cuda):
             break  # free-running greedy decoding parts from the reference's after a near-tie
 
 
+def test_world_of_one_streamed_shards_equal_resident(cuda):
+    """Row e3 on one GPU: the decoder streaming its layer shards from a pinned
+    shard arena through two device slots (the reference's H2D mode, per
+    rank) gives the resident decoder's bits; the profile reports the H2D
+    rate of the rank's stream."""
+
+    from layer_streaming.tensor_parallel import TensorParallelDecoder, TensorParallelWeights
+
+    meta = json.load(open(golden_path("config0.json")))
+    resident = TensorParallelWeights.seeded(1, 0, cuda, seed=meta["weight_seed"])
+    streamed = TensorParallelWeights.seeded(1, 0, cuda, seed=meta["weight_seed"], stream_layers=True)
+    assert streamed.streamed and streamed.arena.storage.is_pinned()
+    assert streamed.arena.nbytes >= 32 * 436_207_616
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    runs = []
+    for weights in (resident, streamed):
+        decoder = TensorParallelDecoder(Config(), weights, top_k=meta["top_k"], profile=True)
+        runs.append(_greedy(decoder, ids, 3))
+        if weights is streamed:
+            prof = decoder.last_stream
+            gbps = prof["h2d_bytes"] / 1e9 / (prof["h2d_event_sum_ms"] / 1000.0)
+            print("streamed shard: {} bytes per step, {:.1f} GB/s H2D, pass {:.1f} ms".format(
+                prof["h2d_bytes"], gbps, prof["gpu_pipeline_ms"]))
+            assert prof["h2d_bytes"] == 2 * sum(unit[3] for unit in streamed.arena.units)
+        decoder.close()
+    for (v1, i1), (v2, i2) in zip(*runs):
+        assert torch.equal(v1, v2) and torch.equal(i1, i2)
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs on the box")
 def test_two_gpu_decoder_reproduces_golden_run():

@@ -163,3 +163,86 @@ def test_sharded_block_and_vocab_topk_match_full(world):
         block_err, topk_ok = results[rank]
         assert block_err < 1e-5, block_err
         assert topk_ok
+
+
+def test_shard_arena_units_are_the_rank_slices():
+    """The streamed shard arena: 4 units per layer in stream order, 256-byte
+    aligned, each piece exactly this rank's slice of the full tensor."""
+
+    full = {}
+    gen = torch.Generator().manual_seed(11)
+    for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
+        key = lo.layer_key(0, name)
+        full[key] = torch.randint(-100, 100, tp.full_shape(key), generator=gen).to(torch.bfloat16)
+    for world in (2, 4):
+        for rank in range(world):
+            arena = tp.ShardArena(world, rank, layers=1, pin=False)
+            assert [u[1] for u in arena.units] == ["qkv", "o_proj", "gate_up", "down_proj"]
+            for key, value in full.items():
+                arena.host_view(key).copy_(tp.shard_tensor(value, key, world, rank))
+            spans = arena.spans()
+            for (layer, name, offset, elements, pieces), (addr, nbytes) in zip(arena.units, spans):
+                assert offset % tp.ShardArena.ALIGN == 0 and nbytes == 2 * elements
+                assert addr == arena.storage.data_ptr() + 2 * offset
+                flat = arena.storage.narrow(0, offset, elements)
+                for key, inner, rows, cols in pieces:
+                    want = tp.shard_tensor(full[key], key, world, rank)
+                    assert want.shape == (rows, cols)
+                    assert torch.equal(flat.narrow(0, inner, rows * cols).view(rows, cols), want)
+            # unit views over a "device slot" (here a host tensor) see the same bytes
+            slot = torch.empty(arena.unit_elements, dtype=torch.bfloat16)
+            _, _, offset, elements, _ = arena.units[2]
+            slot[:elements].copy_(arena.storage.narrow(0, offset, elements))
+            views = arena.views(2, slot)
+            assert torch.equal(views[lo.layer_key(0, "up_proj")],
+                               tp.shard_tensor(full[lo.layer_key(0, "up_proj")], lo.layer_key(0, "up_proj"),
+                                               world, rank))
+
+
+def _stream_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        full = _block_weights()
+        arena = tp.ShardArena(world, rank, layers=1, pin=False)
+        for key, value in full.items():
+            if key.startswith("model."):
+                arena.host_view(key).copy_(tp.shard_tensor(value, key, world, rank).to(torch.bfloat16))
+        # stream the four units through one "slot" in order, as the decoder does
+        slot = torch.empty(arena.unit_elements, dtype=torch.bfloat16)
+        mats = {}
+        for index, (_, _, offset, elements, _) in enumerate(arena.units):
+            slot[:elements].copy_(arena.storage.narrow(0, offset, elements))
+            mats.update({k: v.float().clone() for k, v in arena.views(index, slot).items()})
+        mats["in_norm"], mats["post_norm"] = full["in_norm"], full["post_norm"]
+        x = torch.randn(5, H, generator=torch.Generator().manual_seed(9)) * 0.5
+
+        def reduce(t):
+            t = t.clone()
+            dist.all_reduce(t)
+            return t
+
+        got = _block(x, mats, HEADS // world, KV // world, torch.arange(3, 8), reduce)
+        ref = {k: (v.to(torch.bfloat16).float() if k.startswith("model.") else v) for k, v in full.items()}
+        want = _block(x, ref, HEADS, KV, torch.arange(3, 8), lambda t: t)
+        results[rank] = float((got - want).abs().max() / want.abs().max())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_streamed_shards_give_the_full_block_over_gloo():
+    """Two gloo ranks, each streaming only its shard arena's units, all-reduce
+    to the block of the full (bf16) weights."""
+
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_stream_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    assert all(results[r] < 1e-5 for r in range(2)), dict(results)

@@ -135,7 +135,21 @@ def main():
         decoder = TensorParallelDecoder(Config(), weights, top_k=meta["top_k"], exchange=exchange)
         runs[exchange, "greedy"] = greedy(decoder, ids, 1 + meta["decode_steps"])
         decoder.close()
+    # the streamed mode per rank (row e3): each rank streams only its layer
+    # shards from its pinned shard arena; same bits as the resident shards
+    streamed = TensorParallelWeights.seeded(world, rank, device, seed=meta["weight_seed"], stream_layers=True)
+    decoder = TensorParallelDecoder(Config(), streamed, top_k=meta["top_k"], exchange="peer", profile=True)
+    runs["peer", "streamed"] = run(decoder, device, inputs[:3])
+    prof = decoder.last_stream
+    decoder.close()
+    del streamed
     failures = []
+    for step, (a, b) in enumerate(zip(runs["peer", "streamed"], runs["peer", "forced"])):
+        if not (torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])):
+            failures.append("streamed step {}: differs from the resident shards".format(step))
+    if rank == 0:
+        print("streamed shards: {:.2f} GB per rank per step, {:.1f} GB/s H2D".format(
+            prof["h2d_bytes"] / 1e9, prof["h2d_bytes"] / 1e9 / (prof["h2d_event_sum_ms"] / 1000.0)))
     for key, results in runs.items():
         for step, (values, indices) in enumerate(results):
             both = torch.cat([values.view(torch.int32).to(torch.int64), indices])
