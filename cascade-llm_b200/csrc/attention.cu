@@ -32,6 +32,61 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const __grid
                 smem);
 }
 
+// The same attention with the splits of a (token, KV head) merged inside a
+// thread-block cluster through distributed shared memory (M = 1, splits <=
+// 16): no global partials and no last-CTA ticket. Bit-identical outputs.
+__global__ void __launch_bounds__(kAttnThreads, 2) attention_cluster_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  attention_cta<true>(p, blockIdx.x, blockIdx.y, blockIdx.z,
+                      (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x, smem);
+}
+
+static bool g_cluster_merge = true;
+
+// Launches attention_cluster_kernel; returns kErrUnsupported (nothing
+// launched) when the device cannot hold a cluster of `splits` CTAs.
+static int launch_cluster(const AttnParams& p, int splits, int kv_heads, cudaStream_t stream) {
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    if (cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(AttnSmem::BYTES)) != cudaSuccess) {
+      cudaGetLastError();
+      return kErrUnsupported;
+    }
+    configured_device = dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(splits, kv_heads, 1);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = AttnSmem::BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  int n = 1;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, attention_cluster_kernel, &cfg) != cudaSuccess || clusters < 1) {
+    cudaGetLastError();
+    return kErrUnsupported;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attention_cluster_kernel, p);
+  if (e != cudaSuccess) return fail(kErrCuda, "cb_attention: cluster launch failed: %s", cudaGetErrorString(e));
+  return check_launch("cb_attention");
+}
+
 int prepare_attention() { return configure_smem("cb_attention", attention_kernel, AttnSmem::BYTES); }
 
 }  // namespace cb
@@ -76,8 +131,18 @@ extern "C" int cb_attention(const void* q, const void* k_cache, const void* v_ca
   p.tickets = tickets;
   p.err = error_word();
   p.trace = trace_buffer(&p.trace_tag);
+  if (g_cluster_merge && M == 1 && splits <= kClusterMaxSplits) {
+    const int crc = launch_cluster(p, splits, kv_heads, static_cast<cudaStream_t>(stream));
+    if (crc != kErrUnsupported) return crc;
+  }
   return launch("cb_attention", attention_kernel, dim3(splits, kv_heads, M), dim3(kAttnThreads),
                 AttnSmem::BYTES, static_cast<cudaStream_t>(stream), p);
+}
+
+extern "C" int cb_set_attention_cluster(int enable) {
+  const int previous = g_cluster_merge ? 1 : 0;
+  g_cluster_merge = enable != 0;
+  return previous;
 }
 
 // ============================================================================

@@ -4,6 +4,8 @@
 // of a KV head share one read of every K/V row.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace cb {
@@ -357,12 +359,102 @@ struct ConsumerSync {
   __device__ void operator()() const { named_sync(1, kAttnConsumers); }
 };
 
+// Splits of one (token, KV head) merged inside a thread-block cluster (one
+// CTA per split, the cluster = the head's splits, at most 16): each CTA
+// combines its warps into (m, l) per head and o[4][128] in its own shared
+// memory; after a cluster barrier CTA r merges outputs [r * 512 / S, (r+1) *
+// 512 / S) by reading every split's values through distributed shared
+// memory, and a second barrier keeps each CTA's values alive until all have
+// read them. No global partials, no ticket, no second kernel-wide round trip.
+// The arithmetic is that of attn_publish's merge (same maxima, weights, warp
+// sum of the denominators and fma order over the splits), so the outputs are
+// bit-identical to the global-memory merge.
+constexpr int kClusterMaxSplits = 16;
+static __device__ void attn_publish_cluster(const AttnParams& p, int s, int g, int m, const AttnWarpState* st,
+                                            uint8_t* scratch, float* ring) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const float ninf = -__int_as_float(0x7F800000);
+  float* wm = reinterpret_cast<float*>(scratch + AttnScratch::WML);
+  float* wl = wm + kAttnWarps * kGroup;
+  // this split's combined values, published to the cluster: o [4][128], then (m, l) [4][2]
+  float* cl_o = ring + kAttnWarps * kGroup * kHeadDim;
+  float* cl_ml = cl_o + kGroup * kHeadDim;
+  if (st) {  // the consumer warps (the producer warp passes null)
+    if (lane < kGroup) {
+      wm[warp * kGroup + lane] = st->m_run;
+      wl[warp * kGroup + lane] = st->l_run;
+    }
+    named_sync(1, kAttnConsumers);
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h) {
+      float mm = ninf;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, wm[w * kGroup + h]);
+      const float mw = wm[warp * kGroup + h];
+      const float f = mw == ninf ? 0.f : expf(mw - mm);
+      *reinterpret_cast<float4*>(ring + (warp * kGroup + h) * kHeadDim + 4 * lane) =
+          make_float4(f2lo(st->o[h][0]) * f, f2hi(st->o[h][0]) * f, f2lo(st->o[h][1]) * f, f2hi(st->o[h][1]) * f);
+    }
+    named_sync(1, kAttnConsumers);
+    for (int e = tid; e < kGroup * kHeadDim; e += kAttnConsumers) {
+      const int h = e / kHeadDim, d = e % kHeadDim;
+      float acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) acc += ring[(w * kGroup + h) * kHeadDim + d];
+      cl_o[e] = acc;
+      if (d == 0) {
+        float mm = ninf, ll = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, wm[w * kGroup + h]);
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+          const float mw = wm[w * kGroup + h];
+          ll += mw == ninf ? 0.f : expf(mw - mm) * wl[w * kGroup + h];
+        }
+        cl_ml[2 * h] = mm;
+        cl_ml[2 * h + 1] = ll;
+      }
+    }
+  }
+  cluster.sync();  // every split's (m, l, o) is visible to the cluster
+  const int S = p.splits;
+  float* mg = reinterpret_cast<float*>(scratch + AttnScratch::MRG);
+  float* sm_w = mg;                           // [4][16] weights exp(m_j - M)
+  float* st_L = sm_w + kGroup * kClusterMaxSplits;  // [4] denominators
+  if (warp < kGroup) {  // warp h: maximum, weights and denominator of head h over the splits
+    float2 ml = make_float2(ninf, 0.f);
+    if (lane < S) {
+      const float* r = cluster.map_shared_rank(cl_ml, lane);
+      ml = make_float2(r[2 * warp], r[2 * warp + 1]);
+    }
+    const float mnew = warp_max(ml.x);
+    const float w = ml.x == ninf ? 0.f : expf(ml.x - mnew);
+    if (lane < S) sm_w[warp * kClusterMaxSplits + lane] = w;
+    const float lsum = warp_sum(w * ml.y);
+    if (lane == 0) st_L[warp] = lsum;
+  }
+  __syncthreads();
+  const int per = (kGroup * kHeadDim + S - 1) / S;
+  for (int i = tid; i < per; i += int(blockDim.x)) {
+    const int e = s * per + i;
+    if (e >= kGroup * kHeadDim) break;
+    const int h = e / kHeadDim;
+    float a = 0.f;
+    for (int j = 0; j < S; ++j) a = fmaf(sm_w[h * kClusterMaxSplits + j], cluster.map_shared_rank(cl_o, j)[e], a);
+    p.out[int64_t(m) * p.kv_heads * kGroup * kHeadDim + g * kGroup * kHeadDim + e] = f2bf(a / st_L[h]);
+  }
+  cluster.sync();  // no CTA leaves while others read its shared memory
+}
+
 // One CTA of the split-KV attention, (split s, kv head g, token m): a
 // producer warp streams its positions in 64-position sub-chunks through a
 // 3-stage cp.async.bulk ring; rows of the history (< the step's first
 // position) are fetched before griddepcontrol.wait, rows written by this
 // step's QKV kernel after it. `cta` is the CTA's index in the launch trace.
 // Returns true in thread 0 of the CTA that merged the (token, kv head).
+template <bool kCluster = false>
 static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, unsigned cta, uint8_t* smem) {
   uint16_t* ks = reinterpret_cast<uint16_t*>(smem + AttnSmem::K_OFF);
   uint16_t* vs = reinterpret_cast<uint16_t*>(smem + AttnSmem::V_OFF);
@@ -399,7 +491,7 @@ static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, u
           grid_dep_wait();
           waited = true;
         }
-        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 202)) return false;
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 202)) break;
         const uint32_t bytes = uint32_t(rows) * kHeadDim * 2;
         mbar_arrive_expect_tx(&full[stage], 2 * bytes);
         bulk_g2s(ks + size_t(stage) * kSub * kHeadDim, kbase + t0 * kHeadDim, bytes, &full[stage]);
@@ -410,6 +502,10 @@ static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, u
         }
       }
     }
+    if constexpr (!kCluster) return false;
+    // cluster merge: the producer warp joins the cluster barriers
+    __syncwarp();
+    attn_publish_cluster(p, s, g, m, nullptr, scratch, reinterpret_cast<float*>(ks));
     return false;
   }
 
@@ -441,7 +537,13 @@ static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, u
     }
   }
   const uint64_t t2 = trace_now(p.trace);
-  const bool merged = attn_publish(p, s, g, m, pos0, ws, scratch, reinterpret_cast<float*>(ks), ConsumerSync());
+  bool merged;
+  if constexpr (kCluster) {
+    attn_publish_cluster(p, s, g, m, &ws, scratch, reinterpret_cast<float*>(ks));
+    merged = false;
+  } else {
+    merged = attn_publish(p, s, g, m, pos0, ws, scratch, reinterpret_cast<float*>(ks), ConsumerSync());
+  }
   if (tid == 0) trace_commit(p.trace, p.trace_tag, cta, t0, t1, t2);
   return merged;
 }

@@ -74,6 +74,7 @@ _SIGNATURES = {
         _I, [_P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P, _P, _PP, _I, _I, _I, _I, _P, _P]
     ),
     "cb_attention_workspace_bytes": (_I64, [_I, _I]),
+    "cb_set_attention_cluster": (_I, [_I]),
     "cb_attention": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "cb_attention_noalloc": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _P, _P]),
     "cb_attention_oproj_max_splits": (_I, []),

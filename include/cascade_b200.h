@@ -169,6 +169,12 @@ int cb_topk_merge(const float* a_values, const int64_t* a_indices, int na, const
  * tickets: M*kv_heads uint32 counters, zeroed once by the caller; each launch
  * leaves them zero. */
 int64_t cb_attention_workspace_bytes(int M, int splits);
+/* One-token launches with splits <= 16 merge a KV head's splits inside a
+ * thread-block cluster through distributed shared memory (no use of the
+ * workspace or the tickets; bit-identical outputs) when the device holds
+ * such a cluster; cb_set_attention_cluster(0) selects the global-memory
+ * merge for every launch. Returns the previous setting (default 1). */
+int cb_set_attention_cluster(int enable);
 int cb_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
                  const int32_t* position, int M, int kv_heads, int splits, int chunk, void* out,
                  void* workspace, unsigned int* tickets, void* stream);

@@ -400,3 +400,35 @@ def test_fused_attention_oproj_equals_separate_kernels(ops, cuda, length):
             assert int(err.item()) == 0
     finally:
         lib.cb_set_error_word(None)
+
+
+@pytest.mark.parametrize("length", [1, 37, 300, 2048])
+def test_cluster_merge_equals_global_merge(ops, cuda, length):
+    """One-token launches with splits <= 16 merge inside a thread-block
+    cluster (distributed shared memory); the outputs are bit-identical to the
+    global-memory merge and within SDPA tolerance."""
+
+    from layer_streaming import _native
+
+    lib = _native.lib()
+    kc, vc, k, v = _cache_with_rope(length, length + 64, 90, cuda)
+    q = randn((1, 32, 1, 128), 91).view(4096)
+    pos = torch.tensor([length - 1], dtype=torch.int32, device=cuda)
+    sdpa = lo.attention(q.view(1, 32, 1, 128), k, v, causal=False).view(4096)
+    previous = lib.cb_set_attention_cluster(1)
+    try:
+        for splits in (1, 4, 16):
+            outs = []
+            for cluster in (0, 1):
+                lib.cb_set_attention_cluster(cluster)
+                out = torch.empty(4096, dtype=BF16, device=cuda)
+                ws = torch.empty(ops.attention_workspace_bytes(1, splits), dtype=torch.uint8, device=cuda)
+                tickets = torch.zeros(8, dtype=torch.int32, device=cuda)
+                ops.attention(q, kc, vc, pos, splits, 0, out, ws, tickets)
+                torch.cuda.synchronize()
+                assert int(tickets.abs().sum()) == 0
+                outs.append(out)
+            assert torch.equal(outs[0], outs[1]), splits
+            torch.testing.assert_close(outs[1].float(), sdpa.float(), rtol=2e-2, atol=2e-2)
+    finally:
+        lib.cb_set_attention_cluster(previous)
