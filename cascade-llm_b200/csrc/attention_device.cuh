@@ -524,10 +524,16 @@ static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, u
   int stage = 0;
   uint32_t phase = 0;
   bool failed = false;  // a timed-out wait records the error; control flow is unchanged
+  __shared__ uint64_t trace_sub[2];  // launch trace: first and last sub-chunk in shared memory
+  if (tid == 0) trace_sub[0] = trace_sub[1] = 0;
   for (int i = 0; i < nsub; ++i) {
     const int64_t t0 = start + int64_t(i) * kSub;
     const int rows = int(min(int64_t(kSub), stop - t0));
     if (!failed && !mbar_wait(&full[stage], phase, p.err, 203)) failed = true;
+    if (p.trace && tid == 0) {
+      trace_sub[1] = globaltimer_ns();
+      if (i == 0) trace_sub[0] = trace_sub[1];
+    }
     attn_rows(ks + size_t(stage) * kSub * kHeadDim, vs + size_t(stage) * kSub * kHeadDim, rows, qd, ws, pw);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
@@ -544,7 +550,7 @@ static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, u
   } else {
     merged = attn_publish(p, s, g, m, pos0, ws, scratch, reinterpret_cast<float*>(ks), ConsumerSync());
   }
-  if (tid == 0) trace_commit(p.trace, p.trace_tag, cta, t0, t1, t2);
+  if (tid == 0) trace_commit(p.trace, p.trace_tag, cta, t0, t1, t2, trace_sub[0], trace_sub[1]);
   return merged;
 }
 

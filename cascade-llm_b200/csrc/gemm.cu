@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ====================================================================== host
 using namespace cb;
 
-namespace {
+namespace cb {
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -323,6 +323,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   });
   return fn;
 }
+
+}  // namespace cb
+
+namespace {
 
 // Row-major bf16 matrix [rows, inner] read in [box_rows, 64] tiles with the
 // 128-byte swizzle; rows past the end read as zero.

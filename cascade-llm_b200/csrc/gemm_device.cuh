@@ -10,10 +10,15 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "common.cuh"
 
 namespace cb {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (host;
+// null when the driver does not provide it).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // ----------------------------------------------------------------- TMEM
 // Allocate `cols` TMEM columns (power of two >= 32) for this CTA; the base

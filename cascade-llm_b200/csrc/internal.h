@@ -53,6 +53,9 @@ int prepare_attention();
 int prepare_attention_oproj();
 int prepare_gemm();
 int prepare_prefill_attention();
+int prepare_prefill_attention_tc();
+int run_prefill_attention_tc(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
+                             const int32_t* position, int M, int kv_heads, void* out, cudaStream_t stream);
 
 // Launch `kernel<<<grid, block, smem, stream>>>(args...)` through
 // cudaLaunchKernelEx, adding the programmatic-stream-serialization attribute

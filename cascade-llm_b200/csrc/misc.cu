@@ -241,6 +241,7 @@ extern "C" int cb_prepare(void) {
   if (rc == kOk) rc = prepare_attention_oproj();
   if (rc == kOk) rc = prepare_gemm();
   if (rc == kOk) rc = prepare_prefill_attention();
+  if (rc == kOk) rc = prepare_prefill_attention_tc();
   return rc;
 }
 extern "C" int cb_set_error_word(int32_t* device_word) {

@@ -261,6 +261,14 @@ int prepare_prefill_attention() { return configure_smem("cb_prefill_attention", 
 
 using namespace cb;
 
+static bool g_prefill_tc = true;
+
+extern "C" int cb_set_prefill_attention_tc(int enable) {
+  const int previous = g_prefill_tc ? 1 : 0;
+  g_prefill_tc = enable != 0;
+  return previous;
+}
+
 extern "C" int cb_prefill_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
                                     const int32_t* position, int M, int kv_heads, void* out, void* stream) {
   if (!q || !k_cache || !v_cache || !position || !out)
@@ -270,6 +278,12 @@ extern "C" int cb_prefill_attention(const void* q, const void* k_cache, const vo
   if (M < 1 || kv_heads < 1 || kv_heads > 8 || cache_len < 1)
     return fail(kErrInvalid, "cb_prefill_attention: M=%d kv_heads=%d cache_len=%lld", M, kv_heads,
                 (long long)cache_len);
+  if (g_prefill_tc) {
+    CB_REQUIRE(int64_t(kv_heads) * cache_len < (int64_t(1) << 31),
+               "cb_prefill_attention: kv_heads x cache_len must be < 2^31");
+    return run_prefill_attention_tc(q, k_cache, v_cache, cache_len, position, M, kv_heads, out,
+                                    static_cast<cudaStream_t>(stream));
+  }
   int rc = configure_smem("cb_prefill_attention", prefill_attention_kernel, kSmemPA);
   if (rc != kOk) return rc;
   PrefillAttnParams p = {};

@@ -60,6 +60,7 @@ _SIGNATURES = {
     "cb_gemm_swiglu": (_I, [_P, _I, _P, _P, _I, _P, _P]),
     "cb_prefill_qkv_rope": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _I64, _P]),
     "cb_prefill_attention": (_I, [_P, _P, _P, _I64, _P, _I, _I, _P, _P]),
+    "cb_set_prefill_attention_tc": (_I, [_I]),
     "cb_host_copy": (_I, [_P, _P, _I64, _I]),
     "cb_read_file_ranges": (_I, [ctypes.c_char_p, _I, ctypes.POINTER(_I64), _PP, ctypes.POINTER(_I64), _I]),
     "cb_exchange_bytes": (_I64, []),

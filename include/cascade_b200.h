@@ -259,6 +259,11 @@ int cb_prefill_qkv_rope(const void* xn, int M, const void* wq, const void* wk, c
  * already written). Replaces llama31.py:182-234 for multi-token steps. */
 int cb_prefill_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
                          const int32_t* position, int M, int kv_heads, void* out, void* stream);
+/* Selects the kernel of cb_prefill_attention: 1 (default) tcgen05 MMAs with
+ * S and O in TMEM and TMA-loaded Q/K/V tiles (128 query rows = 32 tokens x
+ * the 4 query heads of a KV head per CTA, 128-position K/V tiles); 0 the
+ * mma.sync kernel (16 tokens per CTA). Returns the previous setting. */
+int cb_set_prefill_attention_tc(int enable);
 
 /* ------------------------------------------------------ tensor parallelism */
 

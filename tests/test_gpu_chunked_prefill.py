@@ -16,9 +16,10 @@ Criteria per step (the north-star ones, tolerance = 2e-2 + 2e-2 * |value|):
     fp32 summation-order difference moves a logit by up to that much, and
     chunked vs single-shot prefill is such a difference);
   * the engine's top-k ids equal to the oracle's at every rank whose gaps to
-    both neighbours exceed the tolerance;
+    both neighbours exceed that widened tolerance (a gap inside the
+    reference's own GPU-vs-CPU distance can flip between its own two paths);
   * the engine's greedy id equal to the oracle's wherever the oracle's
-    top-1/top-2 gap exceeds the tolerance.
+    top-1/top-2 gap exceeds the widened tolerance.
 Every step's ids, values and gaps are printed (``pytest -s``) as the record.
 """
 
@@ -109,10 +110,10 @@ def compare(engine_steps, oracle_steps, label, noise):
         for j in range(len(ov)):
             before = float(ov[j - 1] - ov[j]) if j else float("inf")
             after = float(ov[j] - ov[j + 1]) if j + 1 < len(ov) else 0.0
-            if before > float(tol[j]) and after > float(tol[j]):
+            if before > float(tol[j]) + noise and after > float(tol[j]) + noise:
                 assert int(ei[j]) == int(oi[j]), "{} step {} rank {}: id {} vs oracle {}".format(
                     label, step, j, int(ei[j]), int(oi[j]))
-        if gap > float(tol[0]):
+        if gap > float(tol[0]) + noise:
             assert int(ei[0]) == int(oi[0]), "{} step {}: greedy id {} vs oracle {}".format(
                 label, step, int(ei[0]), int(oi[0]))
     print("{}: worst |dvalue| / (tolerance + noise) = {:.3f}".format(label, worst))

@@ -174,14 +174,46 @@ def _causal_reference(q, k, v, start):
     return torch.softmax(s, dim=-1) @ vf
 
 
+@pytest.mark.parametrize("tc", [1, 0], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("start,m,kv_heads", [(0, 6, 8), (0, 64, 8), (100, 5, 8), (37, 200, 2), (1000, 130, 1),
-                                              (0, 512, 8)])
-def test_prefill_attention_matches_causal_reference(ops, cuda, start, m, kv_heads):
+                                              (0, 512, 8), (5, 33, 8), (4000, 512, 8), (130, 1, 4)])
+def test_prefill_attention_matches_causal_reference(ops, cuda, start, m, kv_heads, tc):
+    """Both prefill attention kernels (tcgen05 with S and O in TMEM, and the
+    mma.sync one) against causal SDPA and the fp32 result; cache rows past
+    the chunk hold NaN (never written), which must not reach the output."""
+
+    from layer_streaming import _native
+
+    previous = _native.lib().cb_set_prefill_attention_tc(tc)
+    try:
+        _prefill_attention_case(ops, cuda, start, m, kv_heads)
+    finally:
+        _native.lib().cb_set_prefill_attention_tc(previous)
+
+
+@pytest.mark.parametrize("tc", [1, 0], ids=["tcgen05", "mma_sync"])
+def test_prefill_attention_maximum_jumps_in_a_later_tile(ops, cuda, tc):
+    """One key in a later 128-position tile aligned with one query row: that
+    row's running maximum jumps (O rescaled for it alone), its neighbours'
+    does not."""
+
+    from layer_streaming import _native
+
+    previous = _native.lib().cb_set_prefill_attention_tc(tc)
+    try:
+        _prefill_attention_case(ops, cuda, 300, 40, 8, spike=True)
+    finally:
+        _native.lib().cb_set_prefill_attention_tc(previous)
+
+
+def _prefill_attention_case(ops, cuda, start, m, kv_heads, spike=False):
     length = start + m
     cap = length + 37
     k = randn((1, kv_heads, length, 128), 1400 + m)
     v = randn((1, kv_heads, length, 128), 1401 + m)
     q = randn((1, 4 * kv_heads, m, 128), 1402 + m)
+    if spike:  # key 200 (tile 1) of KV head 0 = 3 x the query of token 5, head 1
+        k[0, 0, 200] = (3 * q[0, 1, 5].float()).to(BF16)
     kc = torch.full((kv_heads, cap, 128), float("nan"), dtype=BF16, device=cuda)  # past the end: never read
     vc = torch.full_like(kc, float("nan"))
     kc[:, :length] = k[0]
