@@ -116,6 +116,21 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Two floats rounded to nearest-even bf16 and packed (lo in the low half):
+// one cvt instruction (the inputs are finite).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+// 2^x on the special-function unit (denormal results flush to zero: a
+// probability below 2^-126 of the row maximum contributes nothing anyway)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -265,12 +280,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tmem_ld32(s_addr + 32, *reinterpret_cast<float(*)[32]>(v + 32));
       tc_fence_before();
       mbar_arrive(&s_empty[s]);  // S is in registers: the next S_{j+2} may overwrite the buffer
-      float mt = -__int_as_float(0x7F800000);
+      // scale to the log2 domain; mask positions past this row's limit (only
+      // tiles at the end of the causal range have any)
+      const int64_t rel = lim - base;  // column i is visible when i <= rel
+      if (rel >= 63) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        v[i] = base + i <= lim ? v[i] * kTcScaleLog2 : -__int_as_float(0x7F800000);
-        mt = fmaxf(mt, v[i]);
+        for (int i = 0; i < 64; ++i) v[i] *= kTcScaleLog2;
+      } else {
+        const int cut = int(max(int64_t(-1), rel));
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = i <= cut ? v[i] * kTcScaleLog2 : -__int_as_float(0x7F800000);
       }
+      float mx[4] = {v[0], v[1], v[2], v[3]};  // four independent chains
+#pragma unroll
+      for (int i = 4; i < 64; ++i) mx[i & 3] = fmaxf(mx[i & 3], v[i]);
+      float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       xchg[half * kTcRows + r] = mt;
       named_sync(1, 8 * 32);
       mt = fmaxf(mt, xchg[(half ^ 1) * kTcRows + r]);
@@ -280,7 +304,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (j == 0) {
         m_used = mt;
       } else if (mt > m_used + kTcRescale) {
-        alpha = exp2f(m_used - mt);
+        alpha = ex2_approx(m_used - mt);
         m_used = mt;
         rescale = true;
       }
@@ -304,17 +328,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (j >= 2) mbar_wait(&pv_done[s], ((j - 2) >> 1) & 1, p.err, 518);
       // probabilities, their sum, and P (this half = one panel) in the swizzled A layout
       uint8_t* panel = smem + TcSmem::P + s * 2 * kTcPanel + half * kTcPanel;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // fp32 sums of the unrounded probabilities (P is bf16 in the MMA)
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t w[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float p0 = exp2f(v[8 * c + 2 * i] - m_used), p1 = exp2f(v[8 * c + 2 * i + 1] - m_used);
-          l += p0 + p1;  // fp32 sum of the unrounded probabilities (P is bf16 in the MMA, as in SDPA)
-          w[i] = uint32_t(f2bf(p0)) | (uint32_t(f2bf(p1)) << 16);
+          const float p0 = ex2_approx(v[8 * c + 2 * i] - m_used), p1 = ex2_approx(v[8 * c + 2 * i + 1] - m_used);
+          ls[i] += p0 + p1;
+          w[i] = pack_bf16x2(p0, p1);
         }
         *reinterpret_cast<uint4*>(panel + sw128(r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // V rows of never-written cache positions: zero (row r of this half's panel)
       if (int64_t(j) * kTcKV + kTcKV > written) {
         mbar_wait(&v_full[s], (j >> 1) & 1, p.err, 519);
@@ -345,8 +371,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int q = 0; q < 4; ++q) {
         uint32_t w[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          w[i] = uint32_t(f2bf(o[8 * q + 2 * i] * inv)) | (uint32_t(f2bf(o[8 * q + 2 * i + 1] * inv)) << 16);
+        for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(o[8 * q + 2 * i] * inv, o[8 * q + 2 * i + 1] * inv);
         *reinterpret_cast<uint4*>(out + c * 32 + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
