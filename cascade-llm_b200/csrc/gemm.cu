@@ -5,18 +5,21 @@
 // of layer_streaming/llama31.py:238-280 with M > 1), the only place on the
 // path that is tensor-core bound (M >~ 250 tokens at the B200 ridge point).
 //
-// One CTA computes a 128 x BN tile of C:
+// Persistent: one CTA per SM walks the 128 x BN tiles of C (tile t, t + grid,
+// ...; M tiles fastest, so the CTAs working at one time share a few weight
+// tiles and the weights cross HBM about once):
 //   warp 0        TMA producer: A (activations) and W (weights) K-blocks of 64
 //                 bf16, 128-byte swizzle, into a 4-stage shared-memory ring
 //                 (mbarriers full/empty per stage; each CTA loads its own tiles)
+//                 that runs on across tile boundaries
 //   warp 1        MMA issuer: one thread issues tcgen05.mma kind::f16
 //                 (M=128, N=BN, K=16; BF16 in, FP32 accumulate in TMEM) and
 //                 commits each stage back to the producer
-//   warp 2        allocates / frees the BN TMEM columns of the accumulator
+//   warp 2        allocates / frees the TMEM columns of TWO accumulators
 //   warps 4..7    epilogue: tcgen05.ld of their 32 TMEM lanes (= tile rows),
 //                 the mode's fused epilogue, bf16 stores
-// Grid: (M tiles, N tiles), M fastest, so the M tiles of one weight tile are
-// resident at the same time and the weights cross HBM about once.
+// The accumulators alternate between tiles (acc_full / acc_empty mbarriers),
+// so the epilogue of one tile runs while the tensor cores compute the next.
 // Epilogues mirror the decode GEMV's rounding points: plain bf16 store,
 // residual add, SwiGLU (gate and up rows of the same FFN index in one tile),
 // and QKV with RoPE and the K/V cache write.
@@ -51,6 +54,7 @@ constexpr int kGemmThreads = 256;
 
 struct GemmParams {
   int M, N, K;               // N: output columns (SwiGLU: FFN rows)
+  int ntiles;                // tiles along N (the grid walks mtiles x ntiles)
   uint16_t* out;
   float* outf;               // GEMM_PARTIAL: fp32 output (a tensor-parallel partial sum)
   int64_t ld_out;            // output row stride (elements)
@@ -71,8 +75,8 @@ struct GemmSmem {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int BAR = kStages * STAGE;                 // full[S], empty[S], acc
-  static constexpr int TMEM_SLOT = BAR + (2 * kStages + 1) * 8;
+  static constexpr int BAR = kStages * STAGE;                 // full[S], empty[S], acc_full[2], acc_empty[2]
+  static constexpr int TMEM_SLOT = BAR + (2 * kStages + 4) * 8;
   static constexpr int BYTES = TMEM_SLOT + 16 + 1024;         // + slack to align the ring to 1024 B
 };
 
@@ -86,21 +90,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR);
   uint64_t* empty = full + kStages;
-  uint64_t* acc_bar = empty + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::TMEM_SLOT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM;
   const int nk = p.K / kBK;
+  const int mtiles = (p.M + kBM - 1) / kBM;
+  const int tiles = mtiles * p.ntiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_bar, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4 * 32);  // every epilogue thread
+    }
     fence_mbar_init();
   }
-  if (warp == 2) tmem_alloc(tmem_slot, BN);
+  if (warp == 2) tmem_alloc(tmem_slot, 2 * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -111,37 +120,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const CUtensorMap* mb = &tb0;
-      int yb = 0;
-      if (MODE == GEMM_QKV_ROPE) {
-        const int n0 = blockIdx.y * BN;
-        if (n0 < p.q_rows) {
-          yb = n0;
-        } else if (n0 < p.q_rows + p.k_rows) {
-          mb = &tb1;
-          yb = n0 - p.q_rows;
+      int it = 0;  // k-blocks issued so far (the ring position)
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        const int m0 = (tile % mtiles) * kBM, nt = tile / mtiles;
+        const CUtensorMap* mb = &tb0;
+        int yb = 0;
+        if (MODE == GEMM_QKV_ROPE) {
+          const int n0 = nt * BN;
+          if (n0 < p.q_rows) {
+            yb = n0;
+          } else if (n0 < p.q_rows + p.k_rows) {
+            mb = &tb1;
+            yb = n0 - p.q_rows;
+          } else {
+            mb = &tb2;
+            yb = n0 - p.q_rows - p.k_rows;
+          }
+        } else if (MODE == GEMM_SWIGLU) {
+          yb = nt * (BN / 2);
         } else {
-          mb = &tb2;
-          yb = n0 - p.q_rows - p.k_rows;
+          yb = nt * BN;
         }
-      } else if (MODE == GEMM_SWIGLU) {
-        yb = blockIdx.y * (BN / 2);
-      } else {
-        yb = blockIdx.y * BN;
-      }
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t ph = (kb / kStages) & 1;
-        mbar_wait(&empty[s], ph ^ 1, p.err, 401);
-        uint8_t* a_dst = smem + s * L::STAGE;
-        uint8_t* b_dst = a_dst + L::A_BYTES;
-        mbar_arrive_expect_tx(&full[s], L::STAGE);
-        tma_load_2d(a_dst, &ta, kb * kBK, m0, &full[s]);
-        if (MODE == GEMM_SWIGLU) {
-          tma_load_2d(b_dst, &tb0, kb * kBK, yb, &full[s]);
-          tma_load_2d(b_dst + (BN / 2) * kBK * 2, &tb1, kb * kBK, yb, &full[s]);
-        } else {
-          tma_load_2d(b_dst, mb, kb * kBK, yb, &full[s]);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          mbar_wait(&empty[s], ph ^ 1, p.err, 401);
+          uint8_t* a_dst = smem + s * L::STAGE;
+          uint8_t* b_dst = a_dst + L::A_BYTES;
+          mbar_arrive_expect_tx(&full[s], L::STAGE);
+          tma_load_2d(a_dst, &ta, kb * kBK, m0, &full[s]);
+          if (MODE == GEMM_SWIGLU) {
+            tma_load_2d(b_dst, &tb0, kb * kBK, yb, &full[s]);
+            tma_load_2d(b_dst + (BN / 2) * kBK * 2, &tb1, kb * kBK, yb, &full[s]);
+          } else {
+            tma_load_2d(b_dst, mb, kb * kBK, yb, &full[s]);
+          }
         }
       }
     }
@@ -150,157 +163,172 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t ph = (kb / kStages) & 1;
-        mbar_wait(&full[s], ph, p.err, 402);
+      int it = 0, i = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+        const int a = i & 1;
+        // accumulator a is free once the epilogue has read tile i - 2 out of it
+        if (i >= 2) mbar_wait(&acc_empty[a], ((i >> 1) - 1) & 1, p.err, 404);
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * L::STAGE);
-        const uint64_t adesc = umma_desc_sw128(a_addr);
-        const uint64_t bdesc = umma_desc_sw128(a_addr + L::A_BYTES);
+        const uint32_t acc = tmem + a * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          mbar_wait(&full[s], ph, p.err, 402);
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * L::STAGE);
+          const uint64_t adesc = umma_desc_sw128(a_addr);
+          const uint64_t bdesc = umma_desc_sw128(a_addr + L::A_BYTES);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)  // +32 bytes per K step (start address in 16-byte units)
-          umma_bf16(tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
-        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+          for (int k = 0; k < kBK / 16; ++k)  // +32 bytes per K step (start address in 16-byte units)
+            umma_bf16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+        }
+        umma_commit(&acc_full[a]);  // the tile's accumulator is complete
       }
-      umma_commit(acc_bar);  // the accumulator is complete
     }
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
-    mbar_wait(acc_bar, 0, p.err, 403);
-    tc_fence_after();
-    const int row = (warp - 4) * 32 + lane;
-    const int m = m0 + row;
-    const bool live = m < p.M;
-    const uint32_t taddr = tmem + (uint32_t((warp & 3) * 32) << 16);
-    float v[32];
-    if (MODE == GEMM_PARTIAL) {
-      const int n0 = blockIdx.y * BN;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+      const int a = i & 1;
+      mbar_wait(&acc_full[a], (i >> 1) & 1, p.err, 403);
+      tc_fence_after();
+      const int m0 = (tile % mtiles) * kBM, nt = tile / mtiles;
+      const int row = (warp - 4) * 32 + lane;
+      const int m = m0 + row;
+      const bool live = m < p.M;
+      const uint32_t taddr = tmem + a * BN + (uint32_t((warp & 3) * 32) << 16);
+      float v[32];
+      if (MODE == GEMM_PARTIAL) {
+        const int n0 = nt * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_ld32(taddr + c * 32, v);
-        if (!live) continue;
-        float4* o = reinterpret_cast<float4*>(p.outf + int64_t(m) * p.ld_out + n0 + c * 32);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      }
-    } else if (MODE == GEMM_STORE || MODE == GEMM_RESIDUAL || MODE == GEMM_SILU || MODE == GEMM_MUL) {
-      const int n0 = blockIdx.y * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_ld32(taddr + c * 32, v);
-        if (!live) continue;
-        uint16_t* o = p.out + int64_t(m) * p.ld_out + n0 + c * 32;
-        const uint16_t* r = p.residual + int64_t(m) * p.ld_out + n0 + c * 32;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
-          uint4 rr = make_uint4(0, 0, 0, 0);
-          if (MODE == GEMM_RESIDUAL) rr = ld_cg_u4(r + q * 8);
-          if (MODE == GEMM_MUL) rr = ld_cg_u4(o + q * 8);
-          const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float lo = v[q * 8 + 2 * e], hi = v[q * 8 + 2 * e + 1];
-            if (MODE == GEMM_RESIDUAL) {  // x + F.linear(...): the projection rounds to bf16 first
-              lo = bf16lo(rw[e]) + rbf(lo);
-              hi = bf16hi(rw[e]) + rbf(hi);
-            } else if (MODE == GEMM_SILU) {
-              lo = silu_bf16(rbf(lo));
-              hi = silu_bf16(rbf(hi));
-            } else if (MODE == GEMM_MUL) {  // silu(gate) (already bf16) * bf16(up)
-              lo = bf16lo(rw[e]) * rbf(lo);
-              hi = bf16hi(rw[e]) * rbf(hi);
-            }
-            w[e] = uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
-          }
-          *reinterpret_cast<uint4*>(o + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-    } else if (MODE == GEMM_SWIGLU) {
-      const int n0 = blockIdx.y * (BN / 2);
-      float u[32];
-#pragma unroll 1
-      for (int c = 0; c < BN / 64; ++c) {
-        tmem_ld32(taddr + c * 32, v);             // gate rows n0 + c*32 ..
-        tmem_ld32(taddr + BN / 2 + c * 32, u);    // up rows, same FFN index
-        if (!live) continue;
-        uint16_t* o = p.out + int64_t(m) * p.ld_out + n0 + c * 32;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = q * 8 + 2 * e;
-            const float lo = silu_bf16(rbf(v[i])) * rbf(u[i]);
-            const float hi = silu_bf16(rbf(v[i + 1])) * rbf(u[i + 1]);
-            w[e] = uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
-          }
-          *reinterpret_cast<uint4*>(o + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-    } else {  // GEMM_QKV_ROPE, BN == 128: one head per tile
-      const int n0 = blockIdx.y * BN;
-      const int pos = __ldcg(p.pos) + m;
-      const bool in_cache = pos >= 0 && pos < p.cache_len;
-      if (live && n0 >= p.q_rows && !in_cache && p.err) atomicExch(p.err, 103);
-      uint16_t* dst;
-      if (n0 < p.q_rows) {
-        dst = p.out + int64_t(m) * p.ld_out + n0;
-      } else if (n0 < p.q_rows + p.k_rows) {
-        dst = p.k_cache + ((int64_t(n0 - p.q_rows) / 128) * p.cache_len + pos) * 128;
-      } else {
-        dst = p.v_cache + ((int64_t(n0 - p.q_rows - p.k_rows) / 128) * p.cache_len + pos) * 128;
-      }
-      const bool store = live && (n0 < p.q_rows || in_cache);
-      if (n0 >= p.q_rows + p.k_rows) {  // V: no rotation
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < BN / 32; ++c) {
           tmem_ld32(taddr + c * 32, v);
-          if (!store) continue;
+          if (!live) continue;
+          float4* o = reinterpret_cast<float4*>(p.outf + int64_t(m) * p.ld_out + n0 + c * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+      } else if (MODE == GEMM_STORE || MODE == GEMM_RESIDUAL || MODE == GEMM_SILU || MODE == GEMM_MUL) {
+        const int n0 = nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          tmem_ld32(taddr + c * 32, v);
+          if (!live) continue;
+          uint16_t* o = p.out + int64_t(m) * p.ld_out + n0 + c * 32;
+          const uint16_t* r = p.residual + int64_t(m) * p.ld_out + n0 + c * 32;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4];
+            uint4 rr = make_uint4(0, 0, 0, 0);
+            if (MODE == GEMM_RESIDUAL) rr = ld_cg_u4(r + q * 8);
+            if (MODE == GEMM_MUL) rr = ld_cg_u4(o + q * 8);
+            const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float lo = v[q * 8 + 2 * e], hi = v[q * 8 + 2 * e + 1];
+              if (MODE == GEMM_RESIDUAL) {  // x + F.linear(...): the projection rounds to bf16 first
+                lo = bf16lo(rw[e]) + rbf(lo);
+                hi = bf16hi(rw[e]) + rbf(hi);
+              } else if (MODE == GEMM_SILU) {
+                lo = silu_bf16(rbf(lo));
+                hi = silu_bf16(rbf(hi));
+              } else if (MODE == GEMM_MUL) {  // silu(gate) (already bf16) * bf16(up)
+                lo = bf16lo(rw[e]) * rbf(lo);
+                hi = bf16hi(rw[e]) * rbf(hi);
+              }
+              w[e] = uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
+            }
+            *reinterpret_cast<uint4*>(o + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      } else if (MODE == GEMM_SWIGLU) {
+        const int n0 = nt * (BN / 2);
+        float u[32];
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          tmem_ld32(taddr + c * 32, v);             // gate rows n0 + c*32 ..
+          tmem_ld32(taddr + BN / 2 + c * 32, u);    // up rows, same FFN index
+          if (!live) continue;
+          uint16_t* o = p.out + int64_t(m) * p.ld_out + n0 + c * 32;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              w[e] = uint32_t(f2bf(v[q * 8 + 2 * e])) | (uint32_t(f2bf(v[q * 8 + 2 * e + 1])) << 16);
-            *reinterpret_cast<uint4*>(dst + c * 32 + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-      } else {  // Q or K: RoPE on the (d, d + 64) pairs of the head
-        float u[32];
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld32(taddr + c * 32, v);
-          tmem_ld32(taddr + 64 + c * 32, u);
-          if (!store) continue;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t wa[4], wb[4];
-#pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int i = q * 8 + 2 * e;
-              const int d = c * 32 + i;
-              uint16_t a0, b0, a1, b1;
-              rope_pair(v[i], u[i], __ldg(p.inv_freq + d), pos, a0, b0);
-              rope_pair(v[i + 1], u[i + 1], __ldg(p.inv_freq + d + 1), pos, a1, b1);
-              wa[e] = uint32_t(a0) | (uint32_t(a1) << 16);
-              wb[e] = uint32_t(b0) | (uint32_t(b1) << 16);
+              const float lo = silu_bf16(rbf(v[i])) * rbf(u[i]);
+              const float hi = silu_bf16(rbf(v[i + 1])) * rbf(u[i + 1]);
+              w[e] = uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
             }
-            *reinterpret_cast<uint4*>(dst + c * 32 + q * 8) = make_uint4(wa[0], wa[1], wa[2], wa[3]);
-            *reinterpret_cast<uint4*>(dst + 64 + c * 32 + q * 8) = make_uint4(wb[0], wb[1], wb[2], wb[3]);
+            *reinterpret_cast<uint4*>(o + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      } else {  // GEMM_QKV_ROPE, BN == 128: one head per tile
+        const int n0 = nt * BN;
+        const int pos = __ldcg(p.pos) + m;
+        const bool in_cache = pos >= 0 && pos < p.cache_len;
+        if (live && n0 >= p.q_rows && !in_cache && p.err) atomicExch(p.err, 103);
+        uint16_t* dst;
+        if (n0 < p.q_rows) {
+          dst = p.out + int64_t(m) * p.ld_out + n0;
+        } else if (n0 < p.q_rows + p.k_rows) {
+          dst = p.k_cache + ((int64_t(n0 - p.q_rows) / 128) * p.cache_len + pos) * 128;
+        } else {
+          dst = p.v_cache + ((int64_t(n0 - p.q_rows - p.k_rows) / 128) * p.cache_len + pos) * 128;
+        }
+        const bool store = live && (n0 < p.q_rows || in_cache);
+        if (n0 >= p.q_rows + p.k_rows) {  // V: no rotation
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            tmem_ld32(taddr + c * 32, v);
+            if (!store) continue;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                w[e] = uint32_t(f2bf(v[q * 8 + 2 * e])) | (uint32_t(f2bf(v[q * 8 + 2 * e + 1])) << 16);
+              *reinterpret_cast<uint4*>(dst + c * 32 + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        } else {  // Q or K: RoPE on the (d, d + 64) pairs of the head
+          float u[32];
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32(taddr + c * 32, v);
+            tmem_ld32(taddr + 64 + c * 32, u);
+            if (!store) continue;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t wa[4], wb[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = q * 8 + 2 * e;
+                const int d = c * 32 + i;
+                uint16_t a0, b0, a1, b1;
+                rope_pair(v[i], u[i], __ldg(p.inv_freq + d), pos, a0, b0);
+                rope_pair(v[i + 1], u[i + 1], __ldg(p.inv_freq + d + 1), pos, a1, b1);
+                wa[e] = uint32_t(a0) | (uint32_t(a1) << 16);
+                wb[e] = uint32_t(b0) | (uint32_t(b1) << 16);
+              }
+              *reinterpret_cast<uint4*>(dst + c * 32 + q * 8) = make_uint4(wa[0], wa[1], wa[2], wa[3]);
+              *reinterpret_cast<uint4*>(dst + 64 + c * 32 + q * 8) = make_uint4(wb[0], wb[1], wb[2], wb[3]);
+            }
           }
         }
       }
+      // the accumulator is read (tcgen05.wait::ld inside tmem_ld32): hand it back
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);
     }
   }
-  // the accumulator is read (tcgen05.wait::ld inside tmem_ld32): free it
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 
@@ -351,9 +379,10 @@ int run_gemm(const char* what, const CUtensorMap& ta, const CUtensorMap& tb0, co
   int rc = configure_smem(what, gemm_kernel<BN, MODE>, GemmSmem<BN>::BYTES);
   if (rc != kOk) return rc;
   p.err = error_word();
-  // M tiles vary fastest: the CTAs that share a weight tile run together and
-  // read it from DRAM once (L2 serves the others)
-  const dim3 grid((p.M + kBM - 1) / kBM, grid_x);
+  p.ntiles = grid_x;
+  // persistent: one CTA per SM (the shared-memory ring fills the SM), at most one per tile
+  const int64_t tiles = int64_t((p.M + kBM - 1) / kBM) * grid_x;
+  const dim3 grid(unsigned(tiles < sm_count() ? tiles : sm_count()));
   return launch(what, gemm_kernel<BN, MODE>, grid, dim3(kGemmThreads), GemmSmem<BN>::BYTES, stream, ta, tb0, tb1,
                 tb2, p);
 }

@@ -13,16 +13,20 @@
 //                    buffers, so S_{j+1} is computed while S_j is softmaxed)
 //   softmax          8 warps, two threads per TMEM lane (= row), each on
 //                    half the columns: causal mask, running maximum (shared
-//                    through shared memory), exp2, running sum; P_j (bf16)
-//                    written to shared memory in the swizzled K-major layout
-//                    of an MMA A operand
-//   O   += P_j V_j   tcgen05.mma M=128 N=128 K=128 into the TMEM O; V is
-//                    position-major in the cache, so it is the MN-major B
-//                    operand (no transpose)
-// Warp roles: 0 TMA producer (Q once, then K and V tiles through separate
-// 2-stage rings: K_j is reloaded once S_{j-2} has read it, V_j once PV_{j-2}
-// has), 1 MMA issuer (one thread), 2 TMEM allocation, 4-11 softmax and
-// epilogue. The output is O / l per row.
+//                    through shared memory), exp2, running sum; P_j (bf16,
+//                    two per 32-bit column) stored back into TMEM
+//   O   += P_j V_j   tcgen05.mma M=128 N=128 K=128 with A = P read from TMEM
+//                    and B = V from shared memory; V is position-major in
+//                    the cache, so it is the MN-major B operand (no transpose)
+// Keeping P in TMEM leaves shared memory to Q and three-stage K and V rings
+// (TMA latency from L2/HBM is longer than one tile's math), and spares the
+// tensor cores the shared-memory reads of P.
+// Warp roles: 0 TMA producer of Q and the K tiles, 3 TMA producer of the V
+// tiles (separate threads, so a K load never queues behind a V stage that is
+// still being read), 1 MMA issuer (one thread), 2 TMEM allocation, 4-11
+// softmax and epilogue. The output is O / l per row.
+//
+// TMEM columns: S buffers at 0 and 128, O at 256, P buffers at 384 and 448.
 //
 // The running maximum is only moved (and O rescaled in TMEM) when a tile's
 // maximum exceeds it by more than 2^8 in the exp2 domain: the probabilities
@@ -48,9 +52,10 @@ constexpr int kTcTok = 32;                 // tokens per CTA (x 4 heads = 128 ro
 constexpr int kTcRows = 128;
 constexpr int kTcKV = 128;                 // positions per K/V tile
 constexpr int kTcPanel = 128 * 64 * 2;     // one 128-row x 128-byte swizzled panel (16 KB)
-constexpr int kTcStages = 2;
-constexpr int kTcThreads = 384;              // 12 warps: 8 of them softmax
-constexpr uint32_t kTcTmemCols = 512;      // S buffers at 0 and 128, O at 256
+constexpr int kTcStages = 3;               // K and V ring depth
+constexpr int kTcThreads = 384;            // 12 warps: 8 of them softmax
+constexpr uint32_t kTcTmemCols = 512;
+constexpr uint32_t kTcO = 256, kTcP = 384;  // TMEM columns of O and of the two P buffers (64 each)
 constexpr float kTcScaleLog2 = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
 constexpr float kTcRescale = 8.0f;         // move the running maximum when it grows by more than this (log2)
 
@@ -58,14 +63,14 @@ struct TcSmem {
   static constexpr int Q = 0;                                   // 2 panels (dims 0-63, 64-127)
   static constexpr int K = Q + 2 * kTcPanel;                    // per stage 2 panels (dims)
   static constexpr int V = K + kTcStages * 2 * kTcPanel;        // per stage 2 panels (dims)
-  static constexpr int P = V + kTcStages * 2 * kTcPanel;        // 2 buffers x 2 panels (positions 0-63, 64-127)
-  static constexpr int BAR = P + 2 * 2 * kTcPanel;
-  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_empty[2], p_full[2], pv_done[2], o_full
-  static constexpr int NBAR = 18;
+  static constexpr int BAR = V + kTcStages * 2 * kTcPanel;
+  // q_full, k_full[3], k_empty[3], v_full[3], v_empty[3], s_full[2], s_empty[2], p_full[2], pv_done[2], o_full
+  static constexpr int NBAR = 22;
   static constexpr int TMEM_SLOT = BAR + NBAR * 8;
   static constexpr int XCHG = TMEM_SLOT + 16;                   // [2][128] fp32: row maxima / sums of the two halves
   static constexpr int BYTES = XCHG + 2 * 128 * 4 + 1024;       // + slack to align the tiles to 1024 B
 };
+static_assert(TcSmem::BYTES <= 227 * 1024, "prefill attention shared memory");
 
 struct TcParams {
   int M, kv_heads;
@@ -88,6 +93,17 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint3
   return d;
 }
 
+// D[tmem] (+)= A[tmem] * B[smem] for one K=16 step: A is 128 lanes (rows) x
+// 8 columns, each 32-bit column two bf16 of K (the lower one in the low half).
+__device__ __forceinline__ void umma_bf16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y, int z,
                                             uint64_t* bar) {
   asm volatile(
@@ -97,21 +113,42 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+// 32 columns of this thread's TMEM lane without waiting; tmem_ld_wait()
+// waits for every outstanding load and ties the registers to that wait so
+// that no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// 32 words into 32 consecutive columns of this thread's TMEM lane, then wait
+// until the stores are done.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
       "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
       "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
-      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
-      "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
-      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
-      "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
-      "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
-      "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -151,25 +188,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::BAR);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 3;
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 7;
-  uint64_t* s_full = bars + 9;
-  uint64_t* s_empty = bars + 11;
-  uint64_t* p_full = bars + 13;
-  uint64_t* pv_done = bars + 15;
-  uint64_t* o_full = bars + 17;
+  uint64_t* k_empty = k_full + kTcStages;
+  uint64_t* v_full = k_empty + kTcStages;
+  uint64_t* v_empty = v_full + kTcStages;
+  uint64_t* s_full = v_empty + kTcStages;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* o_full = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::TMEM_SLOT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kTcTok, g = blockIdx.y;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kTcStages; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 2 * kTcRows);  // both softmax halves of every row
       mbar_init(&p_full[i], 2 * kTcRows);
@@ -188,28 +227,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int64_t pos0 = __ldcg(p.pos);
   const int64_t span = min(tc_span(p, pos0, t0), p.cache_len);
   const int tiles = int((span + kTcKV - 1) / kTcKV);
+  const int row0 = int(int64_t(g) * p.cache_len);
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ Q and K producer
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, 2 * kTcPanel);
       tma_load_3d(smem + TcSmem::Q, &tq, 0, 4 * g, t0, q_full);
       tma_load_3d(smem + TcSmem::Q + kTcPanel, &tq, 64, 4 * g, t0, q_full);
-      const int row0 = int(int64_t(g) * p.cache_len);
-      for (int j = 0; j < tiles; ++j) {
-        // K_j once S_{j-2} has read the stage, V_j once PV_{j-2} has
-        const int s = j & 1;
-        const int y = row0 + j * kTcKV;
-        if (j >= 2) mbar_wait(&k_empty[s], ((j - 2) >> 1) & 1, p.err, 511);
+      for (int j = 0; j < tiles; ++j) {  // K_j once S_{j-3} has read the stage
+        const int s = j % kTcStages;
+        if (j >= kTcStages) mbar_wait(&k_empty[s], ((j / kTcStages) - 1) & 1, p.err, 511);
         uint8_t* kd = smem + TcSmem::K + s * 2 * kTcPanel;
         mbar_arrive_expect_tx(&k_full[s], 2 * kTcPanel);
-        tma_load_2d(kd, &tk, 0, y, &k_full[s]);
-        tma_load_2d(kd + kTcPanel, &tk, 64, y, &k_full[s]);
-        if (j >= 2) mbar_wait(&v_empty[s], ((j - 2) >> 1) & 1, p.err, 521);
+        tma_load_2d(kd, &tk, 0, row0 + j * kTcKV, &k_full[s]);
+        tma_load_2d(kd + kTcPanel, &tk, 64, row0 + j * kTcKV, &k_full[s]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ V producer
+    if (lane == 0) {
+      for (int j = 0; j < tiles; ++j) {  // V_j once PV_{j-3} has read the stage
+        const int s = j % kTcStages;
+        if (j >= kTcStages) mbar_wait(&v_empty[s], ((j / kTcStages) - 1) & 1, p.err, 521);
         uint8_t* vd = smem + TcSmem::V + s * 2 * kTcPanel;
         mbar_arrive_expect_tx(&v_full[s], 2 * kTcPanel);
-        tma_load_2d(vd, &tv, 0, y, &v_full[s]);
-        tma_load_2d(vd + kTcPanel, &tv, 64, y, &v_full[s]);
+        tma_load_2d(vd, &tv, 0, row0 + j * kTcKV, &v_full[s]);
+        tma_load_2d(vd + kTcPanel, &tv, 64, row0 + j * kTcKV, &v_full[s]);
       }
     }
     __syncwarp();
@@ -221,33 +266,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t q_addr = smem_u32(smem + TcSmem::Q);
       mbar_wait(q_full, 0, p.err, 512);
       auto issue_pv = [&](int j) {
-        mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, 522);
+        const int sv = j % kTcStages;
+        mbar_wait(&v_full[sv], (j / kTcStages) & 1, p.err, 522);
         mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err, 513);
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(smem + TcSmem::P + (j & 1) * 2 * kTcPanel);
-        const uint32_t v_addr = smem_u32(smem + TcSmem::V + (j & 1) * 2 * kTcPanel);
+        const uint32_t p_tmem = tmem + kTcP + (j & 1) * 64;
+        const uint32_t v_addr = smem_u32(smem + TcSmem::V + sv * 2 * kTcPanel);
 #pragma unroll
         for (int k = 0; k < kTcKV / 16; ++k) {
-          const uint64_t adesc = umma_desc_sw128(p_addr + (k >> 2) * kTcPanel + (k & 3) * 32);
           const uint64_t bdesc = umma_desc_sw128_mn(v_addr + k * 16 * 128, kTcPanel, 1024);
-          umma_bf16(tmem + 256, adesc, bdesc, idesc_pv, (j | k) != 0);
+          umma_bf16_tmem_a(tmem + kTcO, p_tmem + k * 8, bdesc, idesc_pv, (j | k) != 0);
         }
         umma_commit(&pv_done[j & 1]);
-        umma_commit(&v_empty[j & 1]);
+        umma_commit(&v_empty[sv]);
       };
       for (int j = 0; j < tiles; ++j) {
-        const int s = j & 1;
-        mbar_wait(&k_full[s], (j >> 1) & 1, p.err, 514);
+        const int sk = j % kTcStages, s = j & 1;
+        mbar_wait(&k_full[sk], (j / kTcStages) & 1, p.err, 514);
         if (j >= 2) mbar_wait(&s_empty[s], ((j - 2) >> 1) & 1, p.err, 515);
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + TcSmem::K + s * 2 * kTcPanel);
+        const uint32_t k_addr = smem_u32(smem + TcSmem::K + sk * 2 * kTcPanel);
 #pragma unroll
         for (int k = 0; k < 128 / 16; ++k) {  // K = the 128 head dims
           const uint32_t off = (k >> 2) * kTcPanel + (k & 3) * 32;
           umma_bf16(tmem + s * kTcKV, umma_desc_sw128(q_addr + off), umma_desc_sw128(k_addr + off), idesc_s, k != 0);
         }
         umma_commit(&s_full[s]);
-        umma_commit(&k_empty[s]);
+        umma_commit(&k_empty[sk]);
         if (j >= 1) issue_pv(j - 1);
       }
       issue_pv(tiles - 1);
@@ -265,36 +310,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // positions <= lim are visible to this row (rows past the chunk act as
     // its last token; their output is not stored)
     const int64_t lim = pos0 + min(t0 + t, p.M - 1);
-    const uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16) + half * 64;
+    const uint32_t row_addr = tmem + (uint32_t(quarter * 32) << 16);
+    const uint32_t lane_addr = row_addr + half * 64;
     const int64_t written = pos0 + p.M;  // cache rows at or past this were never written
     float* xchg = reinterpret_cast<float*>(smem + TcSmem::XCHG);  // [2 halves][128 rows]
     float m_used = -__int_as_float(0x7F800000), l = 0.f;
-    float v[64];
     for (int j = 0; j < tiles; ++j) {
       const int s = j & 1;
       const int64_t base = int64_t(j) * kTcKV + half * 64;
       mbar_wait(&s_full[s], (j >> 1) & 1, p.err, 516);
       tc_fence_after();
-      const uint32_t s_addr = lane_addr + s * kTcKV;
-      tmem_ld32(s_addr, *reinterpret_cast<float(*)[32]>(v));
-      tmem_ld32(s_addr + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+      float v[64];
+      {
+        uint32_t raw[2][32];
+        tmem_ld32_async(lane_addr + s * kTcKV, raw[0]);
+        tmem_ld32_async(lane_addr + s * kTcKV + 32, raw[1]);
+        tmem_ld_wait(raw[0]);
+        tmem_ld_wait(raw[1]);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(raw[i >> 5][i & 31]);
+      }
       tc_fence_before();
       mbar_arrive(&s_empty[s]);  // S is in registers: the next S_{j+2} may overwrite the buffer
-      // scale to the log2 domain; mask positions past this row's limit (only
-      // tiles at the end of the causal range have any)
-      const int64_t rel = lim - base;  // column i is visible when i <= rel
-      if (rel >= 63) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] *= kTcScaleLog2;
-      } else {
+      // mask positions past this row's limit (only tiles at the end of the
+      // causal range have any); column i is visible when i <= rel
+      const int64_t rel = lim - base;
+      if (rel < 63) {
         const int cut = int(max(int64_t(-1), rel));
 #pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = i <= cut ? v[i] * kTcScaleLog2 : -__int_as_float(0x7F800000);
+        for (int i = 0; i < 64; ++i) v[i] = i <= cut ? v[i] : -__int_as_float(0x7F800000);
       }
       float mx[4] = {v[0], v[1], v[2], v[3]};  // four independent chains
 #pragma unroll
       for (int i = 4; i < 64; ++i) mx[i & 3] = fmaxf(mx[i & 3], v[i]);
-      float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * kTcScaleLog2;
       xchg[half * kTcRows + r] = mt;
       named_sync(1, 8 * 32);
       mt = fmaxf(mt, xchg[(half ^ 1) * kTcRows + r]);
@@ -302,7 +351,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool rescale = false;
       float alpha = 1.f;
       if (j == 0) {
-        m_used = mt;
+        m_used = mt;  // finite: position 0 is visible to every row
       } else if (mt > m_used + kTcRescale) {
         alpha = ex2_approx(m_used - mt);
         m_used = mt;
@@ -314,43 +363,45 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (__any_sync(0xFFFFFFFFu, rescale)) {
         mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, 517);
         tc_fence_after();
-        float o[32];
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
-          tmem_ld32(lane_addr + 256 + c * 32, o);
+          uint32_t o[32];
+          tmem_ld32_async(lane_addr + kTcO + c * 32, o);
+          tmem_ld_wait(o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(lane_addr + 256 + c * 32, o);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(lane_addr + kTcO + c * 32, o);
         }
         l *= alpha;
       }
       // the P buffer of tile j - 2 is free once its PV has completed
       if (j >= 2) mbar_wait(&pv_done[s], ((j - 2) >> 1) & 1, p.err, 518);
-      // probabilities, their sum, and P (this half = one panel) in the swizzled A layout
-      uint8_t* panel = smem + TcSmem::P + s * 2 * kTcPanel + half * kTcPanel;
+      // probabilities, their sum, and P (bf16 pairs) into this half's 32 columns of P buffer s
+      const float neg_m = -m_used;
       float ls[4] = {0.f, 0.f, 0.f, 0.f};  // fp32 sums of the unrounded probabilities (P is bf16 in the MMA)
+      uint32_t pw[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float p0 = ex2_approx(v[8 * c + 2 * i] - m_used), p1 = ex2_approx(v[8 * c + 2 * i + 1] - m_used);
-          ls[i] += p0 + p1;
-          w[i] = pack_bf16x2(p0, p1);
-        }
-        *reinterpret_cast<uint4*>(panel + sw128(r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = ex2_approx(fmaf(v[2 * i], kTcScaleLog2, neg_m));
+        const float p1 = ex2_approx(fmaf(v[2 * i + 1], kTcScaleLog2, neg_m));
+        ls[i & 3] += p0 + p1;
+        pw[i] = pack_bf16x2(p0, p1);
       }
+      tc_fence_after();  // ordered after the pv_done wait above (the MMA has read the buffer)
+      tmem_st32(row_addr + kTcP + s * 64 + half * 32, pw);
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // V rows of never-written cache positions: zero (row r of this half's panel)
       if (int64_t(j) * kTcKV + kTcKV > written) {
-        mbar_wait(&v_full[s], (j >> 1) & 1, p.err, 519);
+        const int sv = j % kTcStages;
+        mbar_wait(&v_full[sv], (j / kTcStages) & 1, p.err, 519);
         if (int64_t(j) * kTcKV + r >= written) {
-          uint8_t* vt = smem + TcSmem::V + s * 2 * kTcPanel + half * kTcPanel;
+          uint8_t* vt = smem + TcSmem::V + sv * 2 * kTcPanel + half * kTcPanel;
 #pragma unroll
           for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vt + sw128(r, c)) = make_uint4(0u, 0u, 0u, 0u);
         }
+        fence_proxy_async_smem();  // the zeroed V rows are read by the MMA (async proxy)
       }
-      fence_proxy_async_smem();  // P (and zeroed V rows) are read by the MMA (async proxy)
+      tc_fence_before();  // P (and a rescaled O) before the MMA's PV_j
       mbar_arrive(&p_full[s]);
     }
     // epilogue: O / l for the rows of this chunk's tokens (l = both halves' sums)
@@ -362,16 +413,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool live = t0 + t < p.M;
     const float inv = 1.0f / l;
     uint16_t* out = p.out + (int64_t(t0 + t) * 4 * p.kv_heads + 4 * g + (r & 3)) * 128 + half * 64;
-    float o[32];
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
-      tmem_ld32(lane_addr + 256 + c * 32, o);
+      uint32_t o[32];
+      tmem_ld32_async(lane_addr + kTcO + c * 32, o);
+      tmem_ld_wait(o);
       if (!live) continue;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint32_t w[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(o[8 * q + 2 * i] * inv, o[8 * q + 2 * i + 1] * inv);
+        for (int i = 0; i < 4; ++i)
+          w[i] = pack_bf16x2(__uint_as_float(o[8 * q + 2 * i]) * inv, __uint_as_float(o[8 * q + 2 * i + 1]) * inv);
         *reinterpret_cast<uint4*>(out + c * 32 + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }

@@ -470,12 +470,12 @@ class Llama31DecodeExecutor:
             if self.vocab_runtime is None:
                 values = torch.empty((1, 1, k), dtype=torch.float32, device=self.device)
                 indices = torch.empty((1, 1, k), dtype=torch.int64, device=self.device)
-                logits = None
-                if self.return_full_logits:
-                    logits = torch.empty((1, 1, self.config.vocab_size), dtype=torch.float32, device=self.device)
+                # the last token's logits, always (the reference's resident head
+                # returns every position's [1, M, vocab]; a decode step has M = 1)
+                logits = torch.empty((1, 1, self.config.vocab_size), dtype=torch.float32, device=self.device)
                 ops.lm_head_topk(
                     last, self.resident["model.norm.weight"], self.eps, self.resident["lm_head.weight"], 0, k,
-                    None if logits is None else logits.view(-1), values.view(-1), indices.view(-1),
+                    logits.view(-1), values.view(-1), indices.view(-1),
                     self.lm_workspace, self.lm_ticket,
                 )
             else:

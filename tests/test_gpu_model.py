@@ -166,6 +166,27 @@ def test_eager_and_graph_replay_are_identical(cuda, hbm_engine, meta):
         assert torch.equal(v1, v2) and torch.equal(i1, i2) and torch.equal(l1, l2)
 
 
+def test_resident_head_returns_last_token_logits(cuda, hbm_engine, meta):
+    """Like the reference's resident head (llama31.py:330-339), ``finish``
+    fills ``state.logits`` without being asked: the last token's fp32 row,
+    whose top-k is the returned top-k."""
+
+    import layer_streaming as ls
+
+    _, _, resident, runtime = hbm_engine
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    executor = ls.Llama31DecodeExecutor(Config(), resident, top_k=meta["top_k"])
+    with torch.inference_mode():
+        state = executor.finish(runtime.run(executor, executor.begin(ids)))
+    assert state.logits is not None and tuple(state.logits.shape) == (1, 1, 128256)
+    assert state.logits.dtype == torch.float32
+    values, _ = torch.topk(state.logits[:, -1, :], meta["top_k"], dim=-1)
+    assert torch.equal(values.reshape(-1), state.topk_values.reshape(-1))
+    # (torch.topk orders equal logits arbitrarily: check the ids by lookup)
+    row = state.logits[0, -1]
+    assert torch.equal(row[state.topk_indices.reshape(-1)], state.topk_values.reshape(-1))
+
+
 def test_streamed_runtime_and_vocab_match(cuda, arena, hbm_engine, meta, reference_gpu_topk):
     """The reference's own mode: H2D two-slot streaming + streamed vocab."""
 
