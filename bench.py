@@ -55,6 +55,10 @@ MICRO_BYTES = {
     "down_proj": 4096 * 14336 * 2,
     "lm_head": HEAD_BYTES,
     "attention": 8 * 2048 * 128 * 2 * 2,
+    # int8 weight-only GEMVs: int8 rows + one fp32 scale per row
+    "gate_up_i8": 28672 * 4096 + 28672 * 4,
+    "down_proj_i8": 4096 * 14336 + 4096 * 4,
+    "lm_head_i8": 128256 * 4096 + 128256 * 4,
 }
 
 
@@ -74,6 +78,17 @@ def step_bytes(context):
     return LAYER_BYTES + HEAD_BYTES + NORM_BYTES + 8192 + 131_072 * (context + 1) + 131_072
 
 
+# int8 weight-only decode: half the weight bytes plus one fp32 scale per row
+# (32 layers x (6144 + 4096 + 28672 + 4096) rows, LM head 128256 rows)
+SCALE_BYTES = 4 * (32 * (6144 + 4096 + 28672 + 4096) + 128256)
+
+
+def step_bytes_i8(context):
+    """Algorithmic HBM bytes of one int8 decode token (bf16 KV cache, norms, embedding)."""
+
+    return step_bytes(context) - (LAYER_BYTES + HEAD_BYTES) // 2 + SCALE_BYTES
+
+
 def parse_args():
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -87,11 +102,14 @@ def parse_args():
                         help="BASELINE config 3: each projection at M in {1, 6, 64, 512}, HBM-resident and "
                              "H2D-streamed through two slots (one JSON line per case)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-int8", action="store_true",
+                        help="skip the int8 weight-only decode measurement (a reduced-precision side line)")
     parser.add_argument("--no-streamed", action="store_true", help="skip the H2D-streamed mode measurement")
     parser.add_argument("--profile-range", action="store_true",
                         help="after warm-up, run --steps decode steps between cudaProfilerStart/Stop "
                              "(for `ncu --profile-from-start off`) and exit")
-    parser.add_argument("--micro", choices=sorted(MICRO_BYTES) + sorted(GEMM_SHAPES) + ["prefill_attention"],
+    parser.add_argument("--micro",
+                        choices=sorted(MICRO_BYTES) + sorted(GEMM_SHAPES) + ["prefill_attention", "exchange"],
                         help="time one kernel alone on a small footprint (rotating copies > L2)")
     parser.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
                         help="N>1: tensor-parallel exchange through peer memory inside the projection "
@@ -239,6 +257,28 @@ def time_decode(executor, runtime, token, steps, warmup, barrier):
         torch.cuda.synchronize()
         barrier()
     return start.elapsed_time(end) / steps, token
+
+
+def time_int8(resident, runtime, device, context, steps, warmup):
+    """The optional int8 weight-only mode on the same workload (own executor
+    and KV cache, same seeded weights quantized on the device): a
+    reduced-precision side measurement, never the line's value."""
+
+    import layer_streaming as ls
+
+    executor = ls.Llama31DecodeExecutor(Config(), resident, top_k=10, max_length=context + warmup + steps + 72,
+                                        allow_chunked_prefill=True, decode_weights="int8")
+    token, _ = prefill(executor, runtime, device, context)
+    ms, _ = time_decode(executor, runtime, token, steps, warmup, lambda: None)
+    executor.check_errors()
+    cached = executor.kv_cache.length - steps - 1
+    nbytes = step_bytes_i8(cached)
+    del executor
+    torch.cuda.empty_cache()
+    return {"ms_per_token": round(ms, 4), "bytes_per_token": nbytes,
+            "achieved_gbs": round(nbytes / (ms / 1000.0) / 1e9, 1),
+            "note": "decode_weights='int8' (per-row symmetric int8 weights, fp32 scales; bf16 activations, "
+                    "KV cache and prefill): reduced precision, outside the bf16 parity contract"}
 
 
 def time_e2e(executor, runtime, token, steps):
@@ -486,7 +526,13 @@ def sweep(args, device):
 
     from layer_streaming import _native, ops
 
-    _native.check(_native.lib().cb_prepare(), "cb_prepare")
+    lib = _native.lib()
+    _native.check(lib.cb_prepare(), "cb_prepare")
+    # the executor's split-K registration for chunks of <= 128 tokens
+    split_ws = torch.empty(48 << 18, dtype=torch.float32, device=device)
+    split_tickets = torch.zeros(1024, dtype=torch.int32, device=device)
+    _native.check(lib.cb_set_gemm_workspace(split_ws.data_ptr(), 48 << 20, split_tickets.data_ptr(), 1024),
+                  "cb_set_gemm_workspace")
     bf = torch.bfloat16
     gen = torch.Generator(device=device).manual_seed(9)
     rnd = lambda *shape: (torch.randn(shape, generator=gen, device=device) * 0.02).to(bf)
@@ -559,8 +605,11 @@ def sweep(args, device):
                 free[sl].record(compute)
             torch.cuda.synchronize()
             streamed_us = (time.perf_counter() - started) * 1e6 / n
+            n_out = sum(a for a, _ in mats)
+            k_split = 1 if m == 1 else lib.cb_gemm_split_k(m, k_in, mats[0][0] if name == "gate_up" else n_out,
+                                                          1 if name == "gate_up" else 0)
             print(json.dumps({
-                "sweep": name, "M": m, "weight_bytes": nbytes,
+                "sweep": name, "M": m, "weight_bytes": nbytes, "k_split": k_split,
                 "resident_us": round(resident_us, 2),
                 "resident_gbs": round(nbytes / (resident_us * 1e-6) / 1e9, 1),
                 "resident_tflops": round(flop_per_row * m / (resident_us * 1e-6) / 1e12, 1),
@@ -568,6 +617,7 @@ def sweep(args, device):
                 "streamed_h2d_gbs": round(nbytes / (streamed_us * 1e-6) / 1e9, 2),
             }), flush=True)
         del copies, host, slots
+    lib.cb_set_gemm_workspace(None, 0, None, 0)
 
 
 def micro(args, device):
@@ -583,7 +633,7 @@ def micro(args, device):
         return micro_gemm(args, device)
     if name == "prefill_attention":
         return micro_prefill_attention(args, device)
-    copies = {"lm_head": 2, "gate_up": 2}.get(name, 6)
+    copies = {"lm_head": 2, "gate_up": 2, "lm_head_i8": 3, "gate_up_i8": 4}.get(name, 6)
 
     def rnd(*shape, std=0.02):
         return (torch.randn(shape, device=device) * std).to(bf)
@@ -608,6 +658,31 @@ def micro(args, device):
         mats = [(rnd(14336, 4096), rnd(14336, 4096)) for _ in range(copies)]
         out = torch.empty(14336, dtype=bf, device=device)
         run = lambda m: ops.gate_up_swiglu(x, norm, 1e-5, m[0], m[1], out)
+    elif name.endswith("_i8"):
+        rows, k = {"gate_up_i8": (28672, 4096), "down_proj_i8": (4096, 14336), "lm_head_i8": (128256, 4096)}[name]
+
+        def quantized():
+            w = rnd(rows, k)
+            q = torch.empty((rows, k), dtype=torch.int8, device=device)
+            sc = torch.empty(rows, dtype=torch.float32, device=device)
+            ops.quantize_rows_i8(w, q, sc)
+            return q, sc
+
+        mats = [quantized() for _ in range(copies)]
+        if name == "gate_up_i8":
+            out = torch.empty(14336, dtype=bf, device=device)
+            run = lambda m: ops.gate_up_swiglu_i8(x, norm, 1e-5, m[0][:14336], m[1][:14336], m[0][14336:],
+                                                  m[1][14336:], out)
+        elif name == "down_proj_i8":
+            xin = rnd(14336, std=1.0)
+            res = rnd(4096, std=1.0)
+            run = lambda m: ops.proj_residual_i8(xin, m[0], m[1], res, res)
+        else:
+            values = torch.empty(10, device=device)
+            indices = torch.empty(10, dtype=torch.int64, device=device)
+            ws = torch.empty(ops.lm_head_workspace_bytes(10), dtype=torch.uint8, device=device)
+            ticket = torch.zeros(1, dtype=torch.int32, device=device)
+            run = lambda m: ops.lm_head_topk_i8(x, norm, 1e-5, m[0], m[1], 10, None, values, indices, ws, ticket)
     elif name == "lm_head":
         mats = [rnd(128256, 4096) for _ in range(copies)]
         values = torch.empty(10, device=device)
@@ -642,6 +717,81 @@ def micro(args, device):
     print(json.dumps({"micro": name, "us_per_launch": round(us, 3), "bytes_per_launch": nbytes,
                       "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "peak_kind": kind,
                       "frac": round(gbs / peak, 4), "launches": launches, "copies": len(mats)}), flush=True)
+
+
+def micro_exchange(args, world, rank, local, device):
+    """--micro exchange (any N, under torchrun for N > 1): a rank's o_proj and
+    down_proj shards (K = 4096/N and 14336/N columns) as the local projection
+    (cb_proj_residual) and as the fused projection + peer-memory all-reduce
+    (cb_proj_allreduce_residual), back to back over rotating weight copies;
+    CUDA events, max over ranks. The difference is the exchange's cost."""
+
+    import ctypes
+    import datetime
+
+    import torch.distributed as dist
+
+    from layer_streaming import _native, ops
+    from layer_streaming.tensor_parallel import SLOTS, ExchangeBuffers, _Group
+
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    lib = _native.lib()
+    _native.check(lib.cb_prepare(), "cb_prepare")
+    group = _Group.of(None)
+    buffers = ExchangeBuffers(group, device)
+    epoch = torch.zeros(1, dtype=torch.int32, device=device)
+    bf = torch.bfloat16
+    results = {}
+    stream = _native.stream_ptr(device)
+    for name, full_k in (("o_proj", 4096), ("down_proj", 14336)):
+        k = full_k // world
+        copies = [(torch.randn((4096, k), device=device) * 0.02).to(bf) for _ in range(8)]
+        xin = torch.randn(k, device=device).to(bf)
+        res = torch.randn(4096, device=device).to(bf)
+        out = torch.empty_like(res)
+
+        def local_proj(w):
+            ops.proj_residual(xin, w, res, out)
+
+        slot = [0]
+
+        def fused(w):
+            s = slot[0]
+            _native.check(lib.cb_proj_allreduce_residual(
+                xin.data_ptr(), k, w.data_ptr(), 4096, res.data_ptr(), out.data_ptr(), buffers.pointers,
+                group.rank, group.world, s, SLOTS, epoch.data_ptr(), stream), "cb_proj_allreduce_residual")
+            slot[0] = s + 1
+            if slot[0] == SLOTS:  # one "step": advance the epoch as the decoder does
+                slot[0] = 0
+                ops.position_advance(epoch, 1)
+
+        for label, fn in (("local", local_proj), ("exchange", fused)):
+            for i in range(args.warmup * len(copies)):
+                fn(copies[i % len(copies)])
+            torch.cuda.synchronize()
+            group.barrier()
+            launches = args.steps * SLOTS
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(launches):
+                fn(copies[i % len(copies)])
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / launches], device=device)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            results[name + "_" + label + "_us"] = round(float(t), 3)
+        results[name + "_exchange_cost_us"] = round(results[name + "_exchange_us"] - results[name + "_local_us"], 3)
+        results[name + "_weight_bytes_per_rank"] = 4096 * k * 2
+        results[name + "_nvlink_bytes_per_rank"] = 2 * 4096 * 8 * (world - 1)  # tagged fp32 partials pushed
+        del copies
+    buffers.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({"micro": "exchange", "n_gpus": world, "launches_per_case": args.steps * SLOTS,
+                          **results}), flush=True)
 
 
 def reference_arm(args, rank):
@@ -835,6 +985,7 @@ def tensor_parallel(args, world, rank, local, device):
         },
         "cpu_baseline": None,
         "streamed_mode": streamed,
+        "int8_mode": int8,
         "prefill": {"tokens": args.context, "chunk": 512, "ms": round(prefill_ms, 2),
                     "tokens_per_s": round(args.context / (prefill_ms / 1000.0), 1)},
         "gpu_launches": (1 + 32 * 5 + 1 + 2) * args.steps if args.exchange == "peer" else None,
@@ -859,6 +1010,9 @@ def main():
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.micro == "exchange":
+        micro_exchange(args, world, rank, local, device)
+        return
     if args.micro:
         micro(args, device)
         return
@@ -895,6 +1049,7 @@ def main():
     e2e = time_e2e(executor, runtime, token, args.steps)
     gate_up_ms = time_gate_up(executor, runtime, plan)
     streamed = None if args.no_streamed else time_streamed(plan, store, resident, executor, device, token)
+    int8 = None if args.no_int8 else time_int8(resident, runtime, device, args.context, args.steps, args.warmup)
     peak, peak_kind = measured_peak()
     context = executor.kv_cache.length - args.steps - 1  # mean cached length over the timed steps
     achieved = GATE_UP_BYTES / (gate_up_ms / 1000.0) / 1e9

@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_cluster_kernel(cons
 }
 
 static bool g_cluster_merge = true;
+static int g_min_chunk = 0;  // 0: kMinChunk
 
 // Launches attention_cluster_kernel; returns kErrUnsupported (nothing
 // launched) when the device cannot hold a cluster of `splits` CTAs.
@@ -131,12 +132,21 @@ extern "C" int cb_attention(const void* q, const void* k_cache, const void* v_ca
   p.tickets = tickets;
   p.err = error_word();
   p.trace = trace_buffer(&p.trace_tag);
+  if (M == 1) p.stage = l2_stage_for(1);
+  p.min_chunk = g_min_chunk;
   if (g_cluster_merge && M == 1 && splits <= kClusterMaxSplits) {
     const int crc = launch_cluster(p, splits, kv_heads, static_cast<cudaStream_t>(stream));
     if (crc != kErrUnsupported) return crc;
   }
   return launch("cb_attention", attention_kernel, dim3(splits, kv_heads, M), dim3(kAttnThreads),
                 AttnSmem::BYTES, static_cast<cudaStream_t>(stream), p);
+}
+
+extern "C" int cb_set_attention_min_chunk(int positions) {
+  if (positions < 0 || positions % kSub) return -1;
+  const int previous = g_min_chunk ? g_min_chunk : int(kMinChunk);
+  g_min_chunk = positions;
+  return previous;
 }
 
 extern "C" int cb_set_attention_cluster(int enable) {

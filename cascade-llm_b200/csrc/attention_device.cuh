@@ -33,6 +33,9 @@ struct AttnParams {
   uint64_t* trace;           // per-CTA timeline (cb_set_trace) or null
   uint32_t trace_tag;
   unsigned int* heads_done;  // fused launches: count of merged (token, kv head) outputs, or null
+  int min_chunk;             // least positions per split when chunk == 0 (0: kMinChunk)
+  L2Stage stage;             // a later launch's weights staged into L2 (where: 1 start, 2 after the
+                             // producer's last copy, 3 after the sub-chunk loop, 4 after the merge)
 };
 
 constexpr int kRowsPerWarp = kSub / kAttnWarps;  // 8 rows of a sub-chunk per warp
@@ -59,7 +62,7 @@ __device__ __forceinline__ int64_t attn_chunk(const AttnParams& p, int64_t pos0)
   if (p.chunk > 0) return p.chunk;
   const int64_t longest = min(pos0 + p.M, p.cache_len);
   const int64_t per = (longest + p.splits - 1) / p.splits;
-  return max(kMinChunk, (per + kSub - 1) / kSub * kSub);
+  return max(p.min_chunk > 0 ? int64_t(p.min_chunk) : kMinChunk, (per + kSub - 1) / kSub * kSub);
 }
 
 // Positions [start, stop) of split s for token m, and the sub-chunk count.
@@ -341,6 +344,7 @@ static __device__ bool attn_publish(const AttnParams& p, int s, int g, int m, in
 }
 
 constexpr int kAttnStages = 3;
+__device__ __forceinline__ int attn_ncta() { return int(gridDim.x * gridDim.y * gridDim.z); }
 constexpr int kAttnThreads = kAttnConsumers + 32;  // + one producer warp
 
 struct AttnSmem {
@@ -464,6 +468,7 @@ static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, u
 
   const uint64_t t0 = trace_now(p.trace);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  if (p.stage.where == 1 && warp == 0) l2_stage_issue(p.stage, int(cta), attn_ncta(), lane, 32);
   int64_t pos0, start, stop;
   const int nsub = attn_range(p, s, m, pos0, start, stop);
 
@@ -501,6 +506,7 @@ static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, u
           phase ^= 1;
         }
       }
+      if (p.stage.where == 2) l2_stage_issue(p.stage, int(cta), attn_ncta(), 0, 1);
     }
     if constexpr (!kCluster) return false;
     // cluster merge: the producer warp joins the cluster barriers
@@ -543,6 +549,7 @@ static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, u
     }
   }
   const uint64_t t2 = trace_now(p.trace);
+  if (p.stage.where == 3 && warp == 0) l2_stage_issue(p.stage, int(cta), attn_ncta(), lane, 32);
   bool merged;
   if constexpr (kCluster) {
     attn_publish_cluster(p, s, g, m, &ws, scratch, reinterpret_cast<float*>(ks));
@@ -550,6 +557,7 @@ static __device__ bool attention_cta(const AttnParams& p, int s, int g, int m, u
   } else {
     merged = attn_publish(p, s, g, m, pos0, ws, scratch, reinterpret_cast<float*>(ks), ConsumerSync());
   }
+  if (p.stage.where == 4 && warp == 0) l2_stage_issue(p.stage, int(cta), attn_ncta(), lane, 32);
   if (tid == 0) trace_commit(p.trace, p.trace_tag, cta, t0, t1, t2, trace_sub[0], trace_sub[1]);
   return merged;
 }

@@ -106,6 +106,61 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void bulk_prefetch_l2_hint(const void* src, uint32_t bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(policy)
+               : "memory");
+}
+
+// ------------------------------------------- cross-kernel L2 staging
+// A decode layer is a chain of five dependent kernels; three of them (QKV,
+// attention, o_proj) are latency-bound and leave most of the HBM bandwidth
+// idle, while the fourth (gate+up, 235 MB of weights) is bandwidth-bound.
+// An L2Stage names a slice of that later launch's weights, which the earlier
+// kernels prefetch into L2 while HBM would otherwise idle. The slabs are the
+// consumer launch's two row-major weight matrices (gate rows, up rows), split
+// into `units` row pairs over `ncta` CTAs exactly as the consumer splits them;
+// consumer CTA c's units [u0 + skip, u0 + skip + take) of both slabs are
+// staged (u0 = its first unit; skip = the units it loads before its
+// dependency wait anyway). take == 0 or where == 0: nothing is staged.
+struct L2Stage {
+  const uint8_t* a;   // slab A (gate rows)
+  const uint8_t* b;   // slab B (up rows)
+  int64_t row_bytes;  // bytes per weight row
+  int units, ncta, skip, take;
+  int where;          // issue point inside the issuing kernel (kernel-specific; 0 = off)
+  int policy;         // 0: normal L2 priority, 1: evict_last
+};
+
+// Issue the ranges of issuing CTA i of n, thread t of the nt issuing threads
+// (two ranges, one per slab, per consumer CTA c = i, i + n, ...).
+__device__ __forceinline__ void l2_stage_issue(const L2Stage& s, int i, int n, int t, int nt) {
+  if (s.take <= 0 || s.where == 0) return;
+  const unsigned per = (unsigned(s.ncta) + unsigned(n) - 1u) / unsigned(n);
+  for (unsigned r = unsigned(t); r < 2u * per; r += unsigned(nt)) {
+    const unsigned c = unsigned(i) + unsigned(n) * (r >> 1);
+    if (c >= unsigned(s.ncta)) break;
+    // units * ncta < 2^32 (checked on the host): 32-bit arithmetic
+    const unsigned u0 = unsigned(s.units) * c / unsigned(s.ncta);
+    const unsigned u1 = unsigned(s.units) * (c + 1u) / unsigned(s.ncta);
+    const unsigned lo = min(u0 + unsigned(s.skip), u1), hi = min(lo + unsigned(s.take), u1);
+    if (hi <= lo) continue;
+    const uint8_t* src = ((r & 1u) ? s.b : s.a) + size_t(lo) * size_t(s.row_bytes);
+    const uint32_t bytes = (hi - lo) * uint32_t(s.row_bytes);
+    if (s.policy == 1)
+      bulk_prefetch_l2_hint(src, bytes, policy_evict_last());
+    else
+      bulk_prefetch_l2(src, bytes);
+  }
+}
+
+// Host side (misc.cu): the staging slice that a launch of `kind` (0 QKV,
+// 1 attention, 2 o_proj) carries, from cb_set_l2_stage / _target.
+L2Stage l2_stage_for(int kind);
 
 // ------------------------------------------ programmatic dependent launch
 // wait: block until every prerequisite grid has completed and its memory is
@@ -262,6 +317,60 @@ __device__ __forceinline__ float dot8(const uint4 w, const uint4 x, float acc) {
   acc = fmaf(bf16lo(w.w), bf16lo(x.w), acc);
   acc = fmaf(bf16hi(w.w), bf16hi(x.w), acc);
   return acc;
+}
+
+// ------------------------------------------------------------ int8 weights
+// Exact fp32 value of signed byte b of w: byte b of (w ^ 0x80808080) is
+// b + 128 in [0, 255]; one byte permute places it under the exponent of
+// 2^23 (0x4B0000bb = 2^23 + b + 128), and subtracting 2^23 + 128 leaves b,
+// exactly (every integer below 2^24 is a float). One PRMT and one FADD per
+// weight instead of an integer-to-float conversion.
+template <int B>
+__device__ __forceinline__ float i8_at(uint32_t biased) {
+  return __uint_as_float(__byte_perm(biased, 0x4B000000u, 0x7440u | B)) - 8388736.0f;
+}
+
+// Dot product of 8 int8 weights (two words) with 8 bf16 activations on packed
+// fp32 pairs (sm_100 f32x2 arithmetic): each permuted byte pair becomes two
+// exact integers with one add.rn.f32x2, and one fma.rn.f32x2 accumulates
+// even and odd elements side by side into `acc` {even, odd} - 18
+// instructions per 8 weights instead of 26 with scalar arithmetic.
+__device__ __forceinline__ uint64_t i8_pair(uint32_t biased, int sel_lo, int sel_hi) {
+  const uint32_t lo = __byte_perm(biased, 0x4B000000u, 0x7440u | sel_lo);
+  const uint32_t hi = __byte_perm(biased, 0x4B000000u, 0x7440u | sel_hi);
+  uint64_t p, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(p) : "r"(lo), "r"(hi));
+  // 0xCB000080 = -8388736.0f (2^23 + 128) in both halves
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(p), "l"(0xCB000080CB000080ull));
+  return d;
+}
+__device__ __forceinline__ uint64_t bf16_pair(uint32_t w) {
+  uint64_t p;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(p) : "r"(w << 16), "r"(w & 0xFFFF0000u));
+  return p;
+}
+__device__ __forceinline__ uint64_t dot8_i8x2(const uint2 w, const uint4 x, uint64_t acc) {
+  const uint32_t w0 = w.x ^ 0x80808080u, w1 = w.y ^ 0x80808080u;
+  auto fma2 = [](uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+  };
+  acc = fma2(i8_pair(w0, 0, 1), bf16_pair(x.x), acc);
+  acc = fma2(i8_pair(w0, 2, 3), bf16_pair(x.y), acc);
+  acc = fma2(i8_pair(w1, 0, 1), bf16_pair(x.z), acc);
+  acc = fma2(i8_pair(w1, 2, 3), bf16_pair(x.w), acc);
+  return acc;
+}
+__device__ __forceinline__ float f2sum(uint64_t v) {
+  return __uint_as_float(uint32_t(v)) + __uint_as_float(uint32_t(v >> 32));
+}
+
+// 8-byte streaming load (8 int8 weights), not cached in L1.
+__device__ __forceinline__ uint2 ld_stream8(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
 }
 
 }  // namespace cb

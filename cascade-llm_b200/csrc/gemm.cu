@@ -48,6 +48,8 @@ enum GemmMode : int {
 };
 
 constexpr int kBM = 128;
+constexpr int kSplitMaxTokens = 16;  // split-K chunks: the reduced tile [M][BN] fits shared memory
+constexpr int kMaxSplit = 9;
 constexpr int kBK = 64;
 constexpr int kStages = 4;
 constexpr int kGemmThreads = 256;
@@ -68,6 +70,14 @@ struct GemmParams {
   uint16_t* v_cache;
   int64_t cache_len;
   int* err;
+  // split-K (M <= 16 rows, too few tiles for the SMs): the K blocks of a
+  // tile are split over `ksplit` work items; each stores its fp32 partial
+  // rows into `ws` [tile][ksplit][M][BN], and the last item of a tile to
+  // finish (acq_rel ticket) sums them in slice order into shared memory and
+  // runs the epilogue from there. ksplit == 1: no split.
+  int ksplit;
+  float* ws;
+  unsigned int* tickets;     // [tiles], zero; reset by the reducing item
 };
 
 template <int BN>
@@ -77,7 +87,9 @@ struct GemmSmem {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int BAR = kStages * STAGE;                 // full[S], empty[S], acc_full[2], acc_empty[2]
   static constexpr int TMEM_SLOT = BAR + (2 * kStages + 4) * 8;
-  static constexpr int BYTES = TMEM_SLOT + 16 + 1024;         // + slack to align the ring to 1024 B
+  static constexpr int RED = TMEM_SLOT + 16;                  // split-K: the reduced tile [M <= 16][BN] fp32
+  static constexpr int BYTES = RED + 16 * BN * 4 + 1024;      // + slack to align the ring to 1024 B
+  static_assert(BYTES <= 227 * 1024, "GEMM shared memory");
 };
 
 template <int BN, int MODE>
@@ -97,6 +109,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int nk = p.K / kBK;
   const int mtiles = (p.M + kBM - 1) / kBM;
   const int tiles = mtiles * p.ntiles;
+  const int S = p.ksplit;
+  const int items = tiles * S;  // item w: tile w / S, K slice w % S
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -121,7 +135,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int it = 0;  // k-blocks issued so far (the ring position)
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      for (int w = blockIdx.x; w < items; w += gridDim.x) {
+        const int tile = w / S, ks = w % S;
+        const int kb0 = ks * nk / S, kb1 = (ks + 1) * nk / S;
         const int m0 = (tile % mtiles) * kBM, nt = tile / mtiles;
         const CUtensorMap* mb = &tb0;
         int yb = 0;
@@ -141,7 +157,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         } else {
           yb = nt * BN;
         }
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           mbar_wait(&empty[s], ph ^ 1, p.err, 401);
@@ -164,13 +180,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
       int it = 0, i = 0;
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+      for (int w = blockIdx.x; w < items; w += gridDim.x, ++i) {
+        const int ks = w % S;
+        const int kb0 = ks * nk / S, kb1 = (ks + 1) * nk / S;
         const int a = i & 1;
         // accumulator a is free once the epilogue has read tile i - 2 out of it
         if (i >= 2) mbar_wait(&acc_empty[a], ((i >> 1) - 1) & 1, p.err, 404);
         tc_fence_after();
         const uint32_t acc = tmem + a * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           mbar_wait(&full[s], ph, p.err, 402);
@@ -180,7 +198,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t bdesc = umma_desc_sw128(a_addr + L::A_BYTES);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)  // +32 bytes per K step (start address in 16-byte units)
-            umma_bf16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+            umma_bf16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != kb0) || (k != 0));
           umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
         }
         umma_commit(&acc_full[a]);  // the tile's accumulator is complete
@@ -190,7 +208,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     int i = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+    __shared__ int last_item;  // split-K: this CTA reduces the tile
+    for (int w = blockIdx.x; w < items; w += gridDim.x, ++i) {
+      const int tile = w / S, ks = w % S;
       const int a = i & 1;
       mbar_wait(&acc_full[a], (i >> 1) & 1, p.err, 403);
       tc_fence_after();
@@ -200,11 +220,75 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool live = m < p.M;
       const uint32_t taddr = tmem + a * BN + (uint32_t((warp & 3) * 32) << 16);
       float v[32];
+      if (S > 1) {
+        // this slice's partial rows -> ws; the accumulator is then free
+        float* mine = p.ws + ((int64_t(tile) * S + ks) * p.M + m) * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          tmem_ld32(taddr + c * 32, v);
+          if (!live) continue;
+          float4* o = reinterpret_cast<float4*>(mine + c * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[a]);
+        __threadfence();
+        named_sync(1, 4 * 32);
+        if (warp == 4 && lane == 0)
+          last_item = atom_add_acq_rel_gpu(p.tickets + tile, 1u) == unsigned(S - 1) ? 1 : 0;
+        named_sync(1, 4 * 32);
+        const bool reduce = last_item != 0;
+        named_sync(1, 4 * 32);  // every thread has read the flag before the next item rewrites it
+        if (!reduce) continue;
+        if (warp == 4 && lane == 0) p.tickets[tile] = 0u;
+        // all 128 epilogue threads sum the slices of the whole tile into
+        // shared memory, every slice's load of an output in flight at once
+        // (the sum runs in slice order: the same bits as a per-row sum)
+        float4* red4 = reinterpret_cast<float4*>(smem + L::RED);
+        const float4* src = reinterpret_cast<const float4*>(p.ws + int64_t(tile) * S * p.M * BN);
+        const int64_t slice4 = int64_t(p.M) * BN / 4;
+        for (int o = int(threadIdx.x) - 128; o < p.M * BN / 4; o += 128) {
+          float4 part[kMaxSplit];
+#pragma unroll
+          for (int q = 0; q < kMaxSplit; ++q)
+            if (q < S) part[q] = __ldcg(src + q * slice4 + o);
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int q = 0; q < kMaxSplit; ++q) {
+            if (q < S) {
+              acc.x += part[q].x;
+              acc.y += part[q].y;
+              acc.z += part[q].z;
+              acc.w += part[q].w;
+            }
+          }
+          red4[o] = acc;
+        }
+        named_sync(1, 4 * 32);
+      }
+      // fp32 accumulator columns [col, col + 32) of this thread's row: from
+      // TMEM, or (split-K) from the tile reduced into shared memory
+      auto fetch = [&](int col, float (&dst)[32]) {
+        if (S == 1) {
+          tmem_ld32(taddr + col, dst);
+          return;
+        }
+        const float4* r4 = reinterpret_cast<const float4*>(smem + L::RED) + (int64_t(live ? m : 0) * BN + col) / 4;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 f = r4[j];
+          dst[4 * j] = f.x;
+          dst[4 * j + 1] = f.y;
+          dst[4 * j + 2] = f.z;
+          dst[4 * j + 3] = f.w;
+        }
+      };
       if (MODE == GEMM_PARTIAL) {
         const int n0 = nt * BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(taddr + c * 32, v);
+          fetch(c * 32, v);
           if (!live) continue;
           float4* o = reinterpret_cast<float4*>(p.outf + int64_t(m) * p.ld_out + n0 + c * 32);
 #pragma unroll
@@ -214,7 +298,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int n0 = nt * BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(taddr + c * 32, v);
+          fetch(c * 32, v);
           if (!live) continue;
           uint16_t* o = p.out + int64_t(m) * p.ld_out + n0 + c * 32;
           const uint16_t* r = p.residual + int64_t(m) * p.ld_out + n0 + c * 32;
@@ -248,8 +332,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float u[32];
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
-          tmem_ld32(taddr + c * 32, v);             // gate rows n0 + c*32 ..
-          tmem_ld32(taddr + BN / 2 + c * 32, u);    // up rows, same FFN index
+          fetch(c * 32, v);             // gate rows n0 + c*32 ..
+          fetch(BN / 2 + c * 32, u);    // up rows, same FFN index
           if (!live) continue;
           uint16_t* o = p.out + int64_t(m) * p.ld_out + n0 + c * 32;
 #pragma unroll
@@ -282,7 +366,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (n0 >= p.q_rows + p.k_rows) {  // V: no rotation
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
-            tmem_ld32(taddr + c * 32, v);
+            fetch(c * 32, v);
             if (!store) continue;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -297,8 +381,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float u[32];
 #pragma unroll 1
           for (int c = 0; c < 2; ++c) {
-            tmem_ld32(taddr + c * 32, v);
-            tmem_ld32(taddr + 64 + c * 32, u);
+            fetch(c * 32, v);
+            fetch(64 + c * 32, u);
             if (!store) continue;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -320,8 +404,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       // the accumulator is read (tcgen05.wait::ld inside tmem_ld32): hand it back
-      tc_fence_before();
-      mbar_arrive(&acc_empty[a]);
+      if (S == 1) {
+        tc_fence_before();
+        mbar_arrive(&acc_empty[a]);
+      }
     }
   }
   tc_fence_before();
@@ -373,6 +459,30 @@ int make_tile_map(CUtensorMap* map, const char* what, const void* base, int64_t 
   return kOk;
 }
 
+// Split-K workspace registered by cb_set_gemm_workspace (null: never split).
+float* g_splitk_ws = nullptr;
+int64_t g_splitk_bytes = 0;
+unsigned int* g_splitk_tickets = nullptr;
+int g_splitk_ntickets = 0;
+
+// K slices per tile: 1, unless the chunk is short (M <= 16: one M tile,
+// fewer tiles than SMs) and K is long (>= 8192: the down projection's
+// 14336, 9 slices, 32 tiles -> 288 work items). The count depends on K
+// alone, so every projection with the same K sums the same fp32 slices in
+// the same order. Measured at M = 6 (down 87 -> 40 us), and measured not to
+// pay for K = 4096: a work item costs ~10 us of fixed overhead (partials,
+// ticket, reduce), more than a fifth of a 4096-long tile streams (QKV 48 ->
+// 74 us, gate+up 70 -> 87, o_proj 32.5 -> 32 with 5 slices). A workspace
+// too small for the launch means no split.
+int choose_ksplit(int M, int K, int tiles, int BN) {
+  if (!g_splitk_ws || M > kSplitMaxTokens || tiles >= sm_count() || tiles > g_splitk_ntickets) return 1;
+  if (K / kBK < 128) return 1;
+  const int S = kMaxSplit;
+  if (K / kBK / S < 4) return 1;
+  if (int64_t(tiles) * S * M * BN * 4 > g_splitk_bytes) return 1;
+  return S;
+}
+
 template <int BN, int MODE>
 int run_gemm(const char* what, const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1,
              const CUtensorMap& tb2, GemmParams& p, int grid_x, cudaStream_t stream) {
@@ -380,9 +490,13 @@ int run_gemm(const char* what, const CUtensorMap& ta, const CUtensorMap& tb0, co
   if (rc != kOk) return rc;
   p.err = error_word();
   p.ntiles = grid_x;
-  // persistent: one CTA per SM (the shared-memory ring fills the SM), at most one per tile
+  // persistent: one CTA per SM (the shared-memory ring fills the SM), at most one per work item
   const int64_t tiles = int64_t((p.M + kBM - 1) / kBM) * grid_x;
-  const dim3 grid(unsigned(tiles < sm_count() ? tiles : sm_count()));
+  p.ksplit = choose_ksplit(p.M, p.K, int(tiles), BN);
+  p.ws = p.ksplit > 1 ? g_splitk_ws : nullptr;
+  p.tickets = p.ksplit > 1 ? g_splitk_tickets : nullptr;
+  const int64_t items = tiles * p.ksplit;
+  const dim3 grid(unsigned(items < sm_count() ? items : sm_count()));
   return launch(what, gemm_kernel<BN, MODE>, grid, dim3(kGemmThreads), GemmSmem<BN>::BYTES, stream, ta, tb0, tb1,
                 tb2, p);
 }
@@ -450,6 +564,30 @@ static int gemm_linear(const char* what, int mode, const void* a, int M, int K, 
                      : run_gemm<128, GEMM_STORE>(what, ta, tb, tb, tb, p, N / 128, s);
   return bn == 256 ? run_gemm<256, GEMM_RESIDUAL>(what, ta, tb, tb, tb, p, N / 256, s)
                    : run_gemm<128, GEMM_RESIDUAL>(what, ta, tb, tb, tb, p, N / 128, s);
+}
+
+extern "C" int cb_set_gemm_workspace(void* workspace, int64_t bytes, unsigned int* tickets, int ntickets) {
+  if (!workspace) {
+    g_splitk_ws = nullptr;
+    g_splitk_bytes = 0;
+    g_splitk_tickets = nullptr;
+    g_splitk_ntickets = 0;
+    return kOk;
+  }
+  if (!aligned16(workspace) || bytes < 16 || !tickets || ntickets < 1)
+    return fail(kErrInvalid, "cb_set_gemm_workspace: aligned workspace, bytes and tickets required");
+  g_splitk_ws = static_cast<float*>(workspace);
+  g_splitk_bytes = bytes;
+  g_splitk_tickets = tickets;
+  g_splitk_ntickets = ntickets;
+  return kOk;
+}
+
+extern "C" int cb_gemm_split_k(int M, int K, int N, int swiglu) {
+  const int mtiles = (M + kBM - 1) / kBM;
+  const int bn = swiglu ? 256 : (N % 256 == 0 && int64_t(N / 256) * mtiles >= sm_count()) ? 256 : 128;
+  const int ntiles = swiglu ? N / 128 : N / bn;
+  return choose_ksplit(M, K, mtiles * ntiles, bn);
 }
 
 extern "C" int cb_gemm_bf16(const void* a, int M, int K, const void* w, int N, void* out, void* stream) {

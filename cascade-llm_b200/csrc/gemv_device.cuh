@@ -65,6 +65,11 @@ struct Segment {
   int64_t pos_stride;      // output elements per position (cache writes), 0 otherwise
   int64_t pos_limit;       // cache capacity in positions (cache writes)
   float* outf;             // fp32 output (EPI_PARTIAL)
+  // int8 weights (W8 kernels): the bases above are byte addresses of rows of
+  // K int8 values, and every row has an fp32 scale (weight = int8 x scale),
+  // indexed like the weight rows
+  const float* a_scale;
+  const float* b_scale;
 };
 
 struct GemvParams {
@@ -97,6 +102,7 @@ struct GemvParams {
   uint64_t wait_ns;        // how long a peer's word is awaited before the launch gives up
   uint64_t* trace;         // per-CTA timeline (cb_set_trace) or null
   uint32_t trace_tag;
+  L2Stage stage;           // a later launch's weights staged into L2 (where: 1 start, 2 after the wait, 3 end)
 };
 
 __device__ __forceinline__ int64_t unit_row(const Segment& s, int j) {
@@ -420,8 +426,11 @@ static __device__ void gemv_epilogue(const GemvParams& p, const Segment& sg, int
 
 // DEPTH scales the loads in flight per lane (units per batch); the kernels
 // run DEPTH 1 at 2 CTAs per SM (16 warps, <= 128 registers), which measured
-// faster than DEPTH 2 at 1 CTA per SM with the same bytes in flight.
-template <int K, int DEPTH = 1>
+// faster than DEPTH 2 at 1 CTA per SM with the same bytes in flight. W8:
+// int8 weights, 8-byte loads at the same element positions as the bf16
+// kernel's 16-byte loads, twice the units per batch (the same bytes and
+// registers in flight).
+template <int K, int DEPTH = 1, bool W8 = false>
 struct GemvShape {
   static constexpr int WARPS = kThreads / 32;
   static constexpr int GROUPS = K / 256;        // 512-byte lane groups per row
@@ -434,7 +443,7 @@ struct GemvShape {
   static __device__ __forceinline__ int ulane(unsigned w) { return UL == 1 ? 0 : int(w / WK); }
   static constexpr int KS = K / WK;              // K-slice of each warp
   static constexpr int CPL = KS / 256;           // 16-byte chunks per lane per row slice
-  static constexpr int UB = DEPTH * ((16 / (2 * CPL)) > 0 ? 16 / (2 * CPL) : 1);  // units per warp per batch
+  static constexpr int UB = (W8 ? 2 : 1) * DEPTH * ((16 / (2 * CPL)) > 0 ? 16 / (2 * CPL) : 1);  // units per warp per batch
   // long K-slices keep the activation slice in shared memory (7 chunks = 28
   // registers would otherwise crowd out the weight batch); one region per warp
   static constexpr bool XSMEM = CPL > 4;
@@ -444,9 +453,18 @@ struct GemvShape {
   static_assert(K % 256 == 0 && KS % 256 == 0, "K must be whole 512-byte lane groups");
 };
 
-template <int K, int DEPTH = 1>
+template <bool W8>
+struct WeightChunk {
+  using T = uint4;  // 8 bf16 weights
+};
+template <>
+struct WeightChunk<true> {
+  using T = uint2;  // 8 int8 weights
+};
+
+template <int K, int DEPTH = 1, bool W8 = false>
 struct GemvRegs {
-  uint4 w[GemvShape<K, DEPTH>::UB][2][GemvShape<K, DEPTH>::CPL];
+  typename WeightChunk<W8>::T w[GemvShape<K, DEPTH, W8>::UB][2][GemvShape<K, DEPTH, W8>::CPL];
 };
 
 __device__ __forceinline__ void gemv_locate(const GemvParams& p, int u, int& seg, int& j) {
@@ -458,34 +476,49 @@ __device__ __forceinline__ void gemv_locate(const GemvParams& p, int u, int& seg
   }
 }
 
-// Weight rows of unit u for this lane: row A and row B of the pair.
-template <int K, int DEPTH = 1>
+// Weight rows of unit u for this lane: row A and row B of the pair (element
+// kbase of each row: a bf16 address, or W8 the int8 byte address).
+template <int K, int DEPTH = 1, bool W8 = false>
 __device__ __forceinline__ void gemv_rows(const GemvParams& p, int u, const uint16_t*& ra,
                                           const uint16_t*& rb) {
-  using S = GemvShape<K, DEPTH>;
+  using S = GemvShape<K, DEPTH, W8>;
   int seg, j;
   gemv_locate(p, u, seg, j);
   const Segment& sg = p.seg[seg];
   const int64_t row = int64_t(j / sg.group) * sg.group_stride + (j % sg.group);
   const int kbase = S::kpart(threadIdx.x >> 5) * S::KS + (threadIdx.x & 31) * 8;
-  ra = sg.a_base + row * K + kbase;
-  rb = sg.b_base + row * K + kbase;
+  if constexpr (W8) {
+    ra = reinterpret_cast<const uint16_t*>(reinterpret_cast<const uint8_t*>(sg.a_base) + row * K + kbase);
+    rb = reinterpret_cast<const uint16_t*>(reinterpret_cast<const uint8_t*>(sg.b_base) + row * K + kbase);
+  } else {
+    ra = sg.a_base + row * K + kbase;
+    rb = sg.b_base + row * K + kbase;
+  }
 }
 
-template <int K, int DEPTH = 1>
-__device__ __forceinline__ void gemv_load_batch(const GemvParams& p, int ub, int u1, GemvRegs<K, DEPTH>& r) {
-  using S = GemvShape<K, DEPTH>;
+// Chunk c (elements c * 256 .. of the lane's row slice) of a weight row.
+template <bool W8>
+__device__ __forceinline__ typename WeightChunk<W8>::T ld_chunk(const uint16_t* row, int c) {
+  if constexpr (W8)
+    return ld_stream8(reinterpret_cast<const uint8_t*>(row) + c * 256);
+  else
+    return ld_stream(row + c * 256);
+}
+
+template <int K, int DEPTH = 1, bool W8 = false>
+__device__ __forceinline__ void gemv_load_batch(const GemvParams& p, int ub, int u1, GemvRegs<K, DEPTH, W8>& r) {
+  using S = GemvShape<K, DEPTH, W8>;
   const int ul = S::ulane(threadIdx.x >> 5);
 #pragma unroll
   for (int i = 0; i < S::UB; ++i) {
     const int u = ub + i * S::UL + ul;
     if (u < u1) {
       const uint16_t *ra, *rb;
-      gemv_rows<K, DEPTH>(p, u, ra, rb);
+      gemv_rows<K, DEPTH, W8>(p, u, ra, rb);
 #pragma unroll
       for (int c = 0; c < S::CPL; ++c) {
-        r.w[i][0][c] = ld_stream(ra + c * 256);
-        r.w[i][1][c] = ld_stream(rb + c * 256);
+        r.w[i][0][c] = ld_chunk<W8>(ra, c);
+        r.w[i][1][c] = ld_chunk<W8>(rb, c);
       }
     }
   }
@@ -493,9 +526,10 @@ __device__ __forceinline__ void gemv_load_batch(const GemvParams& p, int ub, int
 
 // Half `half` (registers [half * UB/2, (half + 1) * UB/2)) of the batch whose
 // first unit is ub.
-template <int K, int DEPTH = 1>
-__device__ __forceinline__ void gemv_load_half(const GemvParams& p, int ub, int u1, GemvRegs<K, DEPTH>& r, int half) {
-  using S = GemvShape<K, DEPTH>;
+template <int K, int DEPTH = 1, bool W8 = false>
+__device__ __forceinline__ void gemv_load_half(const GemvParams& p, int ub, int u1, GemvRegs<K, DEPTH, W8>& r,
+                                               int half) {
+  using S = GemvShape<K, DEPTH, W8>;
   constexpr int H = S::UB / 2;
   const int ul = S::ulane(threadIdx.x >> 5);
 #pragma unroll
@@ -503,11 +537,11 @@ __device__ __forceinline__ void gemv_load_half(const GemvParams& p, int ub, int 
     const int u = ub + i * S::UL + ul;
     if ((i >= half * H && i < (half + 1) * H) && u < u1) {
       const uint16_t *ra, *rb;
-      gemv_rows<K, DEPTH>(p, u, ra, rb);
+      gemv_rows<K, DEPTH, W8>(p, u, ra, rb);
 #pragma unroll
       for (int c = 0; c < S::CPL; ++c) {
-        r.w[i][0][c] = ld_stream(ra + c * 256);
-        r.w[i][1][c] = ld_stream(rb + c * 256);
+        r.w[i][0][c] = ld_chunk<W8>(ra, c);
+        r.w[i][1][c] = ld_chunk<W8>(rb, c);
       }
     }
   }
@@ -520,11 +554,11 @@ __device__ __forceinline__ void gemv_cta_units(const GemvParams& p, int cta, int
 
 // Issue the first batch of this CTA's weight loads. Weights never depend on
 // earlier work, so this runs before the dependency wait / grid barrier.
-template <int K, int DEPTH = 1>
-__device__ __forceinline__ void gemv_prefetch(const GemvParams& p, int cta, int ncta, GemvRegs<K, DEPTH>& r) {
+template <int K, int DEPTH = 1, bool W8 = false>
+__device__ __forceinline__ void gemv_prefetch(const GemvParams& p, int cta, int ncta, GemvRegs<K, DEPTH, W8>& r) {
   int u0, u1;
   gemv_cta_units(p, cta, ncta, u0, u1);
-  gemv_load_batch<K, DEPTH>(p, u0, u1, r);
+  gemv_load_batch<K, DEPTH, W8>(p, u0, u1, r);
 }
 
 // CTA-cooperative split-K GEMV over this CTA's contiguous range of units
@@ -535,10 +569,10 @@ __device__ __forceinline__ void gemv_prefetch(const GemvParams& p, int cta, int 
 // barrier the epilogues of all units run in parallel, one thread per unit.
 // The activation slice of a warp stays in registers. `r` holds the first
 // batch issued by gemv_prefetch. Requires the activation row to be complete.
-template <int K, int DEPTH = 1>
-static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int ncta, GemvRegs<K, DEPTH>& r,
+template <int K, int DEPTH = 1, bool W8 = false>
+static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int ncta, GemvRegs<K, DEPTH, W8>& r,
                                 uint64_t* t_loop = nullptr) {
-  using S = GemvShape<K, DEPTH>;
+  using S = GemvShape<K, DEPTH, W8>;
   float* red = reinterpret_cast<float*>(smem + S::RED);
   float* part = reinterpret_cast<float*>(smem + S::SMEM);  // [units][2][WARPS]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
@@ -588,10 +622,15 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
   const int pos = p.pos ? __ldcg(p.pos) + p.token : 0;
   bool pre = false;
   float pre_a = 0.f, pre_b = 0.f, pre_f = 0.f;
+  float sc_a = 1.f, sc_b = 1.f;  // W8: the row scales of this thread's first unit
   if (tid < units) {
     int seg, j;
     gemv_locate(p, u0 + tid, seg, j);
     const Segment& sg = p.seg[seg];
+    if constexpr (W8) {
+      sc_a = __ldg(sg.a_scale + unit_row(sg, j));
+      sc_b = __ldg(sg.b_scale + unit_row(sg, j));
+    }
     if (sg.mode == EPI_RESIDUAL || sg.mode == EPI_MUL || sg.mode == EPI_EXCHANGE) {
       const int64_t oa = int64_t(j / sg.group) * sg.head_stride + (j % sg.group);  // no position stride
       pre_a = bf16f(__ldcg(sg.aux + oa));
@@ -618,17 +657,29 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
 
   // dot products of one batch held in registers
   // dot products of registers [i0, i1) of the batch whose first unit is ub
-  auto consume = [&](const GemvRegs<K, DEPTH>& rr, int ub, int i0, int i1) {
+  auto consume = [&](const GemvRegs<K, DEPTH, W8>& rr, int ub, int i0, int i1) {
 #pragma unroll
     for (int i = 0; i < S::UB; ++i) {
       const int u = ub + i * S::UL + ul;
       if (i >= i0 && i < i1 && u < u1) {
         float a = 0.f, b = 0.f;
+        if constexpr (W8) {
+          uint64_t a2 = 0ull, b2 = 0ull;  // {even, odd} element sums
 #pragma unroll
-        for (int c = 0; c < S::CPL; ++c) {
-          const uint4 xv = S::XSMEM ? xw[c * 32] : xr[S::XSMEM ? 0 : c];
-          a = dot8(rr.w[i][0][c], xv, a);
-          b = dot8(rr.w[i][1][c], xv, b);
+          for (int c = 0; c < S::CPL; ++c) {
+            const uint4 xv = S::XSMEM ? xw[c * 32] : xr[S::XSMEM ? 0 : c];
+            a2 = dot8_i8x2(rr.w[i][0][c], xv, a2);
+            b2 = dot8_i8x2(rr.w[i][1][c], xv, b2);
+          }
+          a = f2sum(a2);
+          b = f2sum(b2);
+        } else {
+#pragma unroll
+          for (int c = 0; c < S::CPL; ++c) {
+            const uint4 xv = S::XSMEM ? xw[c * 32] : xr[S::XSMEM ? 0 : c];
+            a = dot8(rr.w[i][0][c], xv, a);
+            b = dot8(rr.w[i][1][c], xv, b);
+          }
         }
         a = warp_sum(a);
         b = warp_sum(b);
@@ -648,13 +699,13 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
     constexpr int H = S::UB / 2;
     for (int ub = u0; ub < u1; ub += STEP) {
       consume(r, ub, 0, H);
-      if (ub + STEP < u1) gemv_load_half<K, DEPTH>(p, ub + STEP, u1, r, 0);
+      if (ub + STEP < u1) gemv_load_half<K, DEPTH, W8>(p, ub + STEP, u1, r, 0);
       consume(r, ub, H, S::UB);
-      if (ub + STEP < u1) gemv_load_half<K, DEPTH>(p, ub + STEP, u1, r, 1);
+      if (ub + STEP < u1) gemv_load_half<K, DEPTH, W8>(p, ub + STEP, u1, r, 1);
     }
   } else {
     for (int ub = u0; ub < u1; ub += STEP) {
-      if (ub != u0) gemv_load_batch<K, DEPTH>(p, ub, u1, r);
+      if (ub != u0) gemv_load_batch<K, DEPTH, W8>(p, ub, u1, r);
       consume(r, ub, 0, S::UB);
     }
   }
@@ -671,6 +722,11 @@ static __device__ void gemv_run(const GemvParams& p, uint8_t* smem, int cta, int
     int seg, j;
     gemv_locate(p, u0 + i, seg, j);
     const Segment& sg = p.seg[seg];
+    if constexpr (W8) {  // int8 rows: dot of the integers times the row scale
+      const int64_t row = unit_row(sg, j);
+      a *= i == tid ? sc_a : __ldg(sg.a_scale + row);
+      b *= i == tid ? sc_b : __ldg(sg.b_scale + row);
+    }
     if (sg.mode == EPI_TOPK) {
       const float la = rbf(a), lb = rbf(b);  // F.linear(...) is bf16, then .float()
       const int64_t row = int64_t(j / sg.group) * sg.group_stride + (j % sg.group);
@@ -749,11 +805,13 @@ int finish_params(GemvParams& p);
 int build_qkv_params(GemvParams& p, const void* x, const void* norm_w, float eps, const void* wq,
                      const void* wk, const void* wv, const float* inv_freq, const int32_t* position,
                      int token, void* q_out, void* k_cache, void* v_cache, int64_t cache_len, int q_heads,
-                     int kv_heads);
+                     int kv_heads, int wbytes = 2, const float* sq = nullptr, const float* sk = nullptr,
+                     const float* sv = nullptr);
 int build_residual_params(GemvParams& p, const void* x, int K, const void* w, int N, const void* residual,
-                          void* out);
+                          void* out, int wbytes = 2, const float* scale = nullptr);
 int build_gate_up_params(GemvParams& p, const char* what, const void* x, const void* norm_w, float eps,
-                         const void* w_gate, const void* w_up, int N, int mode, void* out, const void* aux);
+                         const void* w_gate, const void* w_up, int N, int mode, void* out, const void* aux,
+                         int wbytes = 2, const float* s_gate = nullptr, const float* s_up = nullptr);
 int gemv_grid_size();
 
 }  // namespace cb

@@ -33,6 +33,8 @@ bool pdl_enabled();
 // Wall-clock limit of the tensor-parallel exchange waits (cb_set_exchange_wait_ns).
 uint64_t exchange_wait_ns();
 int sm_count();
+// Grid of every GEMV launch (two CTAs per SM).
+int gemv_grid_size();
 // The launch-trace buffer set by cb_set_trace (null: tracing off) and, when
 // set, the next launch tag.
 uint64_t* trace_buffer(uint32_t* tag);

@@ -58,6 +58,31 @@ int sm_count() {
 
 int32_t* error_word() { return g_error_word; }
 
+// Cross-kernel L2 staging (cb_set_l2_stage, cb_set_l2_stage_target): the
+// issue point and size per issuing kernel kind, and the weights that
+// launches issued while a target is set stage.
+struct StageKnob {
+  int where, take, skip, policy;
+};
+// Default: the attention kernel stages 10 row pairs per gate+up CTA after its
+// sub-chunk loop (decode step at 2K context 3.053 -> 3.015 ms/token; every
+// other issue point measured slower or no faster).
+static StageKnob g_stage_knob[3] = {{0, 0, 0, 0}, {3, 10, 4, 0}, {0, 0, 0, 0}};
+static L2Stage g_stage_target = {};
+
+L2Stage l2_stage_for(int kind) {
+  L2Stage s = g_stage_target;
+  if (kind < 0 || kind > 2 || !s.a || g_stage_knob[kind].where == 0 || g_stage_knob[kind].take <= 0) {
+    s = L2Stage{};
+    return s;
+  }
+  s.where = g_stage_knob[kind].where;
+  s.take = g_stage_knob[kind].take;
+  s.skip = g_stage_knob[kind].skip;
+  s.policy = g_stage_knob[kind].policy;
+  return s;
+}
+
 int configure_smem_raw(const char* what, const void* kernel, size_t bytes) {
   static std::mutex lock;
   static std::set<std::pair<const void*, int>> done;
@@ -235,6 +260,30 @@ extern "C" uint64_t cb_set_exchange_wait_ns(uint64_t ns) {
   return g_exchange_wait_ns.exchange(ns ? ns : 2000000000ull);
 }
 extern "C" int cb_sm_count(void) { return sm_count(); }
+extern "C" int cb_set_l2_stage(int kind, int where, int take, int skip, int policy) {
+  if (kind < 0 || kind > 2 || where < 0 || where > 4 || take < 0 || skip < 0 || policy < 0 || policy > 1)
+    return fail(kErrInvalid, "cb_set_l2_stage: kind=%d where=%d take=%d skip=%d policy=%d", kind, where, take,
+                skip, policy);
+  g_stage_knob[kind] = StageKnob{where, take, skip, policy};
+  return kOk;
+}
+extern "C" int cb_set_l2_stage_target(const void* w_a, const void* w_b, int units, int K) {
+  if (!w_a) {
+    g_stage_target = L2Stage{};
+    return kOk;
+  }
+  if (!w_b || units < 1 || K < 8 || K % 8 || !aligned16(w_a) || !aligned16(w_b) ||
+      int64_t(units) * (gemv_grid_size() + 1) >= (int64_t(1) << 32) || int64_t(units) * K * 2 >= (int64_t(1) << 32))
+    return fail(kErrInvalid, "cb_set_l2_stage_target: bad slabs (units=%d, K=%d)", units, K);
+  L2Stage s = {};
+  s.a = static_cast<const uint8_t*>(w_a);
+  s.b = static_cast<const uint8_t*>(w_b);
+  s.row_bytes = int64_t(K) * 2;
+  s.units = units;
+  s.ncta = gemv_grid_size();
+  g_stage_target = s;
+  return kOk;
+}
 extern "C" int cb_prepare(void) {
   int rc = prepare_gemv();
   if (rc == kOk) rc = prepare_attention();

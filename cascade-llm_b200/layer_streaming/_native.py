@@ -35,6 +35,8 @@ _SIGNATURES = {
     "cb_prepare": (_I, []),
     "cb_set_error_word": (_I, [_P]),
     "cb_set_trace": (_I, [_P]),
+    "cb_set_l2_stage": (_I, [_I, _I, _I, _I, _I]),
+    "cb_set_l2_stage_target": (_I, [_P, _P, _I, _I]),
     "cb_stream_key": (ctypes.c_uint64, [ctypes.c_uint64, ctypes.c_char_p]),
     "cb_fill_normal_bf16": (_I, [_P, _I64, _I64, ctypes.c_uint64, ctypes.c_double, _P]),
     "cb_fill_bf16": (_I, [_P, _I64, _F, _P]),
@@ -51,6 +53,11 @@ _SIGNATURES = {
     "cb_up_mul": (_I, [_P, _P, _F, _P, _P, _P]),
     "cb_lm_head_workspace_bytes": (_I64, [_I]),
     "cb_lm_head_topk": (_I, [_P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P, _P, _P, _P]),
+    "cb_quantize_rows_i8": (_I, [_P, _I64, _I, _P, _P, _P]),
+    "cb_qkv_rope_i8": (_I, [_P, _P, _F, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _I64, _I, _I, _P]),
+    "cb_proj_residual_i8": (_I, [_P, _I, _P, _P, _I, _P, _P, _P]),
+    "cb_gate_up_swiglu_i8": (_I, [_P, _P, _F, _P, _P, _P, _P, _I, _P, _P]),
+    "cb_lm_head_topk_i8": (_I, [_P, _P, _F, _P, _P, _I64, _I64, _I, _P, _P, _P, _P, _P, _P]),
     "cb_topk_merge": (_I, [_P, _P, _I, _P, _P, _I, _I, _P, _P, _P]),
     "cb_gemm_bf16": (_I, [_P, _I, _I, _P, _I, _P, _P]),
     "cb_gemm_residual": (_I, [_P, _I, _I, _P, _I, _P, _P, _P]),
@@ -76,6 +83,9 @@ _SIGNATURES = {
     ),
     "cb_attention_workspace_bytes": (_I64, [_I, _I]),
     "cb_set_attention_cluster": (_I, [_I]),
+    "cb_set_attention_min_chunk": (_I, [_I]),
+    "cb_set_gemm_workspace": (_I, [_P, ctypes.c_int64, _P, _I]),
+    "cb_gemm_split_k": (_I, [_I, _I, _I, _I]),
     "cb_attention": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "cb_attention_noalloc": (_I, [_P, _P, _P, _I64, _P, _I, _I, _I, _P, _P]),
     "cb_attention_oproj_max_splits": (_I, []),

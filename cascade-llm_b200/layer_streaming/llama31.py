@@ -49,6 +49,11 @@ _UNIT_OPS = {
     "gate_up": ("gate_up",),
 }
 _TOPK_MAX = 64
+# prefill chunks of at most this many tokens split the GEMMs' K range (one
+# 128-row tile leaves most SMs idle); workspace and per-tile tickets
+_SPLIT_K_MAX_TOKENS = 16
+_SPLIT_K_BYTES = 16 << 20
+_SPLIT_K_TICKETS = 1024
 _DEFAULT_CAPACITY = 8192
 
 
@@ -198,7 +203,7 @@ class Llama31DecodeExecutor:
 
     def __init__(self, config, resident, kv_cache=None, vocab_runtime=None, top_k=10,
                  return_full_logits=False, max_length=None, allow_chunked_prefill=False,
-                 use_graphs=True):
+                 use_graphs=True, decode_weights=None):
         expected = {
             "hidden_size": 4096,
             "intermediate_size": 14336,
@@ -249,6 +254,16 @@ class Llama31DecodeExecutor:
         self.fuse_attention = os.environ.get("CASCADE_B200_FUSED_ATTENTION", "0") == "1"
         self._fused_max_splits = int(lib.cb_attention_oproj_max_splits())
         self._graphs = {}
+        # layer -> (gate, up) device views of the HBM-resident runtime `_stage_owner`; `_stage_active`
+        # is set only while run_units_resident issues a one-token step
+        self._stage_slabs, self._stage_owner, self._stage_active = {}, None, False
+        self._split_k_ws = self._split_k_tickets = None
+        # optional int8 weight-only one-token steps (HBM-resident runtimes):
+        # key -> (int8 [N, K], fp32 scales [N]) quantized from `_i8_owner`'s views
+        self.decode_weights = decode_weights or os.environ.get("CASCADE_B200_DECODE_WEIGHTS", "bf16")
+        if self.decode_weights not in ("bf16", "int8"):
+            raise ValueError("decode_weights must be 'bf16' or 'int8'")
+        self._i8, self._i8_owner, self._i8_active, self._i8_step = {}, None, False, False
         self._rows = 0
         self._buffers(1)
         self._attn_ws = None
@@ -310,6 +325,7 @@ class Llama31DecodeExecutor:
             raise ValueError("input_ids is empty")
         if past and tokens != 1 and not self.allow_chunked_prefill:
             raise ValueError("after prefill, only one-token decode calls are supported")
+        self._i8_step = False  # set by run_units_resident for an int8 one-token step
         with torch.cuda.device(self.device):
             if position_ids is not None:
                 start = int(position_ids.reshape(-1)[0])
@@ -339,7 +355,22 @@ class Llama31DecodeExecutor:
         )
 
     def _unit(self, layer, operation, weights, splits=None, chunk=None, fused=None):
+        if 1 < self._tokens <= _SPLIT_K_MAX_TOKENS:
+            # the registration lives only for this unit's launches: the
+            # workspace belongs to this executor
+            self._register_split_k()
+            try:
+                return self._unit_ops(layer, operation, weights, splits, chunk, fused)
+            finally:
+                _native.lib().cb_set_gemm_workspace(None, 0, None, 0)
+        return self._unit_ops(layer, operation, weights, splits, chunk, fused)
+
+    def _unit_ops(self, layer, operation, weights, splits=None, chunk=None, fused=None):
         tokens = self._tokens
+        if tokens == 1 and self._i8_active:
+            if splits is None:
+                splits, chunk, fused = self.attention_config(1, self.kv_cache.length + 1)
+            return self._unit_i8(layer, operation, splits, chunk)
         cache = self.kv_cache
         eps = self.eps
         pos = cache.position
@@ -350,6 +381,8 @@ class Llama31DecodeExecutor:
         kc, vc = cache.key(layer), cache.value(layer)
         # multi-token steps (prefill) run the fused units as tcgen05 GEMMs
         gemm = tokens > 1
+        if not gemm and self._stage_active:
+            self._stage_target(layer, operation)
         if operation in ("qkv", "q_proj", "k_proj", "v_proj") and gemm:
             wq = w("q_proj") if operation in ("qkv", "q_proj") else None
             wk = w("k_proj") if operation in ("qkv", "k_proj") else None
@@ -411,6 +444,94 @@ class Llama31DecodeExecutor:
         else:
             raise ValueError("unknown Llama operation {}".format(operation))
 
+    def _collect_int8(self, runtime):
+        """Quantize every decode weight matrix of `runtime` (and the resident
+        LM head) to int8 rows with fp32 scales, once, on the device."""
+
+        q8 = {}
+        with torch.cuda.device(self.device):
+            for index in range(len(runtime.plan.units)):
+                for key, t in runtime.unit_views(index).items():
+                    if t.dim() == 2 and key not in q8:
+                        q = torch.empty(t.shape, dtype=torch.int8, device=self.device)
+                        scale = torch.empty(t.shape[0], dtype=torch.float32, device=self.device)
+                        ops.quantize_rows_i8(t, q, scale)
+                        q8[key] = (q, scale)
+            if self.vocab_runtime is None:
+                head = self.resident["lm_head.weight"]
+                q = torch.empty(head.shape, dtype=torch.int8, device=self.device)
+                scale = torch.empty(head.shape[0], dtype=torch.float32, device=self.device)
+                ops.quantize_rows_i8(head, q, scale)
+                q8["lm_head.weight"] = (q, scale)
+        self._i8, self._i8_owner = q8, id(runtime)
+
+    def _unit_i8(self, layer, operation, splits, chunk):
+        """One-token unit with int8 weights (the bf16 kernels' fused epilogues)."""
+
+        cache, eps, pos, res = self.kv_cache, self.eps, self.kv_cache.position, self.resident
+        q8 = lambda name: self._i8[_matrix_key(layer, name)]
+        kc, vc = cache.key(layer), cache.value(layer)
+        if operation == "qkv":
+            (wq, sq), (wk, sk), (wv, sv) = q8("q_proj"), q8("k_proj"), q8("v_proj")
+            ops.qkv_rope_i8(self._x[0], res["model.layers.{}.input_layernorm.weight".format(layer)], eps, wq, sq,
+                            wk, sk, wv, sv, self.inv_freq, pos, 0, self._q[0], kc, vc)
+        elif operation == "o_proj":
+            ws = self._attention_workspace(1, splits)
+            ops.attention(self._q[:1], kc, vc, pos, splits, chunk, self._attn[:1], ws, self._tickets)
+            wo, so = q8("o_proj")
+            ops.proj_residual_i8(self._attn[0], wo, so, self._x[0], self._x[0])
+        elif operation == "gate_up":
+            (wg, sg), (wu, su) = q8("gate_proj"), q8("up_proj")
+            ops.gate_up_swiglu_i8(self._x[0], res["model.layers.{}.post_attention_layernorm.weight".format(layer)],
+                                  eps, wg, sg, wu, su, self._mlp[0])
+        elif operation == "down_proj":
+            wd, sd = q8("down_proj")
+            ops.proj_residual_i8(self._mlp[0], wd, sd, self._x[0], self._x[0])
+        else:
+            raise ValueError("int8 decode weights need the matrix_group or layer granularity (got {})".format(
+                operation))
+
+    def _register_split_k(self):
+        """Short chunks (a few-token prompt): let the prefill GEMMs split K over
+        the SMs (``cb_set_gemm_workspace``) through this executor's fp32
+        workspace and zeroed per-tile tickets, allocated on first use."""
+
+        if self._split_k_ws is None:
+            self._split_k_ws = torch.empty(_SPLIT_K_BYTES // 4, dtype=torch.float32, device=self.device)
+            self._split_k_tickets = torch.zeros(_SPLIT_K_TICKETS, dtype=torch.int32, device=self.device)
+        _native.check(
+            _native.lib().cb_set_gemm_workspace(self._split_k_ws.data_ptr(), _SPLIT_K_BYTES,
+                                                self._split_k_tickets.data_ptr(), _SPLIT_K_TICKETS),
+            "cb_set_gemm_workspace",
+        )
+
+    def _stage_target(self, layer, operation):
+        """One-token steps with HBM-resident weights: the QKV, attention and
+        o_proj launches of a layer may pre-stage that layer's gate+up weights
+        into L2 (``cb_set_l2_stage``); the target is set before the layer's
+        QKV and cleared before its gate+up."""
+
+        if operation == "qkv":
+            slabs = self._stage_slabs.get(layer)
+            if slabs is not None:
+                wg, wu = slabs
+                _native.check(
+                    _native.lib().cb_set_l2_stage_target(wg.data_ptr(), wu.data_ptr(), wg.shape[0], wg.shape[1]),
+                    "cb_set_l2_stage_target",
+                )
+        elif operation in ("gate_up", "gate_proj"):
+            _native.lib().cb_set_l2_stage_target(None, None, 0, 0)
+
+    def _collect_stage_slabs(self, runtime):
+        slabs = {}
+        for index, unit in enumerate(runtime.plan.units):
+            views = runtime.unit_views(index)
+            gate = _matrix_key(unit.layer_index, "gate_proj")
+            up = _matrix_key(unit.layer_index, "up_proj")
+            if gate in views and up in views:
+                slabs[unit.layer_index] = (views[gate], views[up])
+        self._stage_slabs, self._stage_owner = slabs, id(runtime)
+
     def _after_last_unit(self):
         # the step's K/V are cached: advance the device position counter
         ops.position_advance(self.kv_cache.position, self._tokens)
@@ -433,9 +554,21 @@ class Llama31DecodeExecutor:
         """All units of a step with HBM-resident weights (graph replay for M=1)."""
 
         units = runtime.plan.units
+        if self._tokens == 1 and self._stage_owner != id(runtime):
+            self._collect_stage_slabs(runtime)
+        i8 = self._tokens == 1 and self.decode_weights == "int8"
+        if i8 and self._i8_owner != id(runtime):
+            self._collect_int8(runtime)
+        self._i8_step = i8
         if not self.use_graphs or self._tokens != 1:
-            for index, unit in enumerate(units):
-                state = self(unit, runtime.unit_views(index), state)
+            self._stage_active = self._tokens == 1 and not i8
+            self._i8_active = i8
+            try:
+                for index, unit in enumerate(units):
+                    state = self(unit, runtime.unit_views(index), state)
+            finally:
+                self._stage_active = self._i8_active = False
+                _native.lib().cb_set_l2_stage_target(None, None, 0, 0)
             return state
         length = self.kv_cache.length + 1
         bucket = max(64, 1 << (length - 1).bit_length())
@@ -451,9 +584,15 @@ class Llama31DecodeExecutor:
             with torch.cuda.graph(graph):
                 if embed:
                     self._embed_one()
-                for index, unit in enumerate(units):
-                    for operation in _UNIT_OPS.get(unit.operation, (unit.operation,)):
-                        self._unit(unit.layer_index, operation, runtime.unit_views(index), splits, chunk, fused)
+                self._stage_active = not i8
+                self._i8_active = i8
+                try:
+                    for index, unit in enumerate(units):
+                        for operation in _UNIT_OPS.get(unit.operation, (unit.operation,)):
+                            self._unit(unit.layer_index, operation, runtime.unit_views(index), splits, chunk, fused)
+                finally:
+                    self._stage_active = self._i8_active = False
+                    _native.lib().cb_set_l2_stage_target(None, None, 0, 0)
                 ops.position_advance(self.kv_cache.position, 1)
             self.kv_cache.length = saved
             self._graphs[key] = graph
@@ -473,11 +612,17 @@ class Llama31DecodeExecutor:
                 # the last token's logits, always (the reference's resident head
                 # returns every position's [1, M, vocab]; a decode step has M = 1)
                 logits = torch.empty((1, 1, self.config.vocab_size), dtype=torch.float32, device=self.device)
-                ops.lm_head_topk(
-                    last, self.resident["model.norm.weight"], self.eps, self.resident["lm_head.weight"], 0, k,
-                    logits.view(-1), values.view(-1), indices.view(-1),
-                    self.lm_workspace, self.lm_ticket,
-                )
+                if self._i8_step:
+                    head, scale = self._i8["lm_head.weight"]
+                    ops.lm_head_topk_i8(last, self.resident["model.norm.weight"], self.eps, head, scale, k,
+                                        logits.view(-1), values.view(-1), indices.view(-1), self.lm_workspace,
+                                        self.lm_ticket)
+                else:
+                    ops.lm_head_topk(
+                        last, self.resident["model.norm.weight"], self.eps, self.resident["lm_head.weight"], 0, k,
+                        logits.view(-1), values.view(-1), indices.view(-1),
+                        self.lm_workspace, self.lm_ticket,
+                    )
             else:
                 normed = torch.empty((1, 1, 4096), dtype=torch.bfloat16, device=self.device)
                 ops.rmsnorm(last, self.resident["model.norm.weight"], self.eps, normed.view(-1))

@@ -63,6 +63,22 @@ _SCHEMAS = {
         "Tensor(a!)? q_out, Tensor(b!)? k_cache, Tensor(c!)? v_cache, int q_heads=32, int kv_heads=8) -> ()"
     ),
     "position_advance": "position_advance(Tensor(a!) position, int count) -> ()",
+    "quantize_rows_i8": "quantize_rows_i8(Tensor w, Tensor(a!) q, Tensor(b!) scale) -> ()",
+    "qkv_rope_i8": (
+        "qkv_rope_i8(Tensor x, Tensor? norm_w, float eps, Tensor wq, Tensor sq, Tensor wk, Tensor sk, "
+        "Tensor wv, Tensor sv, Tensor inv_freq, Tensor position, int token, Tensor(a!) q_out, "
+        "Tensor(b!) k_cache, Tensor(c!) v_cache) -> ()"
+    ),
+    "proj_residual_i8": "proj_residual_i8(Tensor x, Tensor w, Tensor scale, Tensor residual, Tensor(a!) out) -> ()",
+    "gate_up_swiglu_i8": (
+        "gate_up_swiglu_i8(Tensor x, Tensor? norm_w, float eps, Tensor w_gate, Tensor s_gate, Tensor w_up, "
+        "Tensor s_up, Tensor(a!) out) -> ()"
+    ),
+    "lm_head_topk_i8": (
+        "lm_head_topk_i8(Tensor x, Tensor? norm_w, float eps, Tensor w, Tensor scale, int k, "
+        "Tensor(a!)? logits, Tensor(b!) out_values, Tensor(c!) out_indices, Tensor(d!) workspace, "
+        "Tensor(e!) ticket) -> ()"
+    ),
 }
 
 
@@ -384,6 +400,70 @@ def memcpy_h2d_async(dst, src):
     nat.check(
         nat.lib().cb_memcpy_h2d_async(dst.data_ptr(), src.data_ptr(), nbytes, _stream(dst)),
         "cascade.memcpy_h2d_async",
+    )
+
+
+# ------------------------------------------------ int8 weight-only decode
+# Optional reduced-precision mode (outside the bf16 parity contract): each
+# weight matrix is an int8 [N, K] tensor plus fp32 row scales [N].
+I8 = torch.int8
+F32 = torch.float32
+
+
+def quantize_rows_i8(w, q, scale):
+    nat.check(
+        nat.lib().cb_quantize_rows_i8(
+            nat.ptr(w, BF16, "w"), w.shape[0], w.shape[1], nat.ptr(q, I8, "q"), nat.ptr(scale, F32, "scale"),
+            _stream(w),
+        ),
+        "cascade.quantize_rows_i8",
+    )
+
+
+def qkv_rope_i8(x, norm_w, eps, wq, sq, wk, sk, wv, sv, inv_freq, position, token, q_out, k_cache, v_cache):
+    nat.check(
+        nat.lib().cb_qkv_rope_i8(
+            nat.ptr(x, BF16, "x"), nat.ptr(norm_w, BF16, "norm_w"), float(eps),
+            nat.ptr(wq, I8, "wq"), nat.ptr(sq, F32, "sq"), nat.ptr(wk, I8, "wk"), nat.ptr(sk, F32, "sk"),
+            nat.ptr(wv, I8, "wv"), nat.ptr(sv, F32, "sv"), nat.ptr(inv_freq, F32, "inv_freq"),
+            nat.ptr(position, torch.int32, "position"), int(token), nat.ptr(q_out, BF16, "q_out"),
+            nat.ptr(k_cache, BF16, "k_cache"), nat.ptr(v_cache, BF16, "v_cache"), k_cache.shape[-2],
+            wq.shape[0] // 128, wk.shape[0] // 128, _stream(x),
+        ),
+        "cascade.qkv_rope_i8",
+    )
+
+
+def proj_residual_i8(x, w, scale, residual, out):
+    nat.check(
+        nat.lib().cb_proj_residual_i8(
+            nat.ptr(x, BF16, "x"), w.shape[1], nat.ptr(w, I8, "w"), nat.ptr(scale, F32, "scale"), w.shape[0],
+            nat.ptr(residual, BF16, "residual"), nat.ptr(out, BF16, "out"), _stream(x),
+        ),
+        "cascade.proj_residual_i8",
+    )
+
+
+def gate_up_swiglu_i8(x, norm_w, eps, w_gate, s_gate, w_up, s_up, out):
+    nat.check(
+        nat.lib().cb_gate_up_swiglu_i8(
+            nat.ptr(x, BF16, "x"), nat.ptr(norm_w, BF16, "norm_w"), float(eps),
+            nat.ptr(w_gate, I8, "w_gate"), nat.ptr(s_gate, F32, "s_gate"), nat.ptr(w_up, I8, "w_up"),
+            nat.ptr(s_up, F32, "s_up"), w_gate.shape[0], nat.ptr(out, BF16, "out"), _stream(x),
+        ),
+        "cascade.gate_up_swiglu_i8",
+    )
+
+
+def lm_head_topk_i8(x, norm_w, eps, w, scale, k, logits, out_values, out_indices, workspace, ticket):
+    nat.check(
+        nat.lib().cb_lm_head_topk_i8(
+            nat.ptr(x, BF16, "x"), nat.ptr(norm_w, BF16, "norm_w"), float(eps), nat.ptr(w, I8, "w"),
+            nat.ptr(scale, F32, "scale"), w.shape[0], 0, int(k), nat.ptr(logits, F32, "logits"),
+            nat.ptr(out_values, F32, "out_values"), nat.ptr(out_indices, torch.int64, "out_indices"),
+            nat.ptr(workspace, None, "workspace"), nat.ptr(ticket, torch.int32, "ticket"), _stream(x),
+        ),
+        "cascade.lm_head_topk_i8",
     )
 
 

@@ -54,6 +54,27 @@ int cb_set_error_word(int32_t* device_word);
  * from 0 per cb_set_trace call, in issue order (a captured graph replays its
  * tags). NULL (the default) turns tracing off. */
 int cb_set_trace(void* device_buffer);
+/* Cross-kernel L2 staging of a decode layer's gate+up weights. No
+ * counterpart in the reference (an HBM-residency scheduling hint of this
+ * engine). The QKV, attention and o_proj launches of a layer are
+ * latency-bound and leave HBM mostly idle, while the gate+up projection that
+ * follows them streams 235 MB; launches of kind `kind` (0 QKV, 1 one-token
+ * attention, 2 o_proj = cb_proj_residual with K = N = 4096) issued while a
+ * target is set prefetch into L2 `take` units (row pairs) per gate+up CTA,
+ * after the `skip` units that CTA loads before its dependency wait anyway.
+ * `where` is the issue point (0 off; GEMV: 1 before the dependency wait,
+ * 2 after it, 3 at the end; attention: 1 at the start, 2 after the last
+ * K/V copy is issued, 3 after the sub-chunk loop, 4 after the merge);
+ * `policy` 0 normal, 1 evict_last L2 priority. Default: the attention
+ * kernel stages 10 row pairs per gate+up CTA after its sub-chunk loop
+ * (kind 1: where 3, take 10, skip 4); QKV and o_proj stage nothing. */
+int cb_set_l2_stage(int kind, int where, int take, int skip, int policy);
+/* The gate+up slabs (gate rows, up rows: `units` rows of K bf16 each) that
+ * launches issued from now on stage; w_gate NULL clears the target. A
+ * captured graph keeps the target of its capture. The target is
+ * process-wide: clear it before the slabs are freed (the executor sets it
+ * for the launches of one step and clears it after them). */
+int cb_set_l2_stage_target(const void* w_gate, const void* w_up, int units, int K);
 
 /* ---------------------------------------------------------------- set-up */
 
@@ -175,6 +196,11 @@ int64_t cb_attention_workspace_bytes(int M, int splits);
  * such a cluster; cb_set_attention_cluster(0) selects the global-memory
  * merge for every launch. Returns the previous setting (default 1). */
 int cb_set_attention_cluster(int enable);
+/* Least positions per split when cb_attention sizes the splits on the device
+ * (chunk = 0): a multiple of 64; 0 restores the default (128). Affects
+ * launches issued from now on. Returns the previous value, or -1 (nothing
+ * changed) for an invalid one. */
+int cb_set_attention_min_chunk(int positions);
 int cb_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_len,
                  const int32_t* position, int M, int kv_heads, int splits, int chunk, void* out,
                  void* workspace, unsigned int* tickets, void* stream);
@@ -241,6 +267,29 @@ int cb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache
  *                        caches [kv_heads, cache_len, 128] (K after RoPE); any of
  *                        wq / wk / wv may be NULL (the `matrix` granularity) */
 int cb_gemm_bf16(const void* a, int M, int K, const void* w, int N, void* out, void* stream);
+/* Split-K for short chunks (M <= 16, fewer output tiles than SMs, e.g. a
+ * 6-token prompt: 32 down_proj tiles on 148 SMs): registers the fp32
+ * workspace and the zeroed per-tile tickets that the prefill GEMMs above use
+ * to split a tile's K range into 9 slices when K >= 8192 (the down
+ * projection; the count depends on K only, so projections of equal K give
+ * the same bits however they are grouped into launches; shorter K is not
+ * split, measured slower); the last CTA of a tile (acquire-release ticket)
+ * sums the slices' partials in slice order, runs the fused epilogue and
+ * resets the ticket (the tile is summed into shared memory by all epilogue
+ * threads at once). A launch splits only when the workspace holds tiles x
+ * slices x M x (128 or 256) floats (9 MB covers every Llama-3.1-8B
+ * projection at M = 16) and `ntickets` >= its tiles.
+ * The registration is process-wide and outlives nothing: unregister (NULL)
+ * before the workspace or the tickets are freed, or a later launch writes
+ * into freed memory (the executor registers around each short prefill unit
+ * and unregisters after it). Launches captured in a CUDA graph keep the
+ * registration of their capture; concurrent launches on different streams
+ * must not share a workspace.
+ * NULL turns splitting off (the default). No counterpart in the reference,
+ * which runs these projections through cuBLAS. cb_gemm_split_k returns the
+ * slice count a launch of that shape would use (swiglu: N = FFN rows). */
+int cb_set_gemm_workspace(void* workspace, int64_t bytes, unsigned int* tickets, int ntickets);
+int cb_gemm_split_k(int M, int K, int N, int swiglu);
 int cb_gemm_residual(const void* a, int M, int K, const void* w, int N, const void* residual, void* out,
                      void* stream);
 int cb_gemm_partial(const void* a, int M, int K, const void* w, int N, float* out, void* stream);
@@ -264,6 +313,36 @@ int cb_prefill_attention(const void* q, const void* k_cache, const void* v_cache
  * the 4 query heads of a KV head per CTA, 128-position K/V tiles); 0 the
  * mma.sync kernel (16 tokens per CTA). Returns the previous setting. */
 int cb_set_prefill_attention_tc(int enable);
+
+/* ------------------------------------------------ int8 weights (optional) */
+
+/* Low-precision weight transfer: int8 weight-only decode projections. No
+ * counterpart in the reference, whose README lists INT8/INT4 weight transfer
+ * as not supported (README.md:156); this reduced-precision mode is outside
+ * the bf16 parity contract and is never the benchmark's headline value.
+ * Row r of an [N, K] matrix is K int8 values q and an fp32 scale s_r, with
+ * w ~= q * s_r:
+ *   cb_quantize_rows_i8: s_r = max|w_r| / 127 (fp32 division), q =
+ *       round-half-even(w / s_r) clamped to [-127, 127] (fp32 division); an
+ *       all-zero row gets s_r = 0, q = 0. w: bf16 [rows, K], K a multiple of
+ *       256; q: int8 [rows, K] (16-byte aligned); scale: fp32 [rows].
+ * The projections below are the bf16 entry points of the same names with
+ * each weight matrix replaced by (int8 matrix, its row scales): the row's
+ * integer dot product with the bf16 activations is accumulated in fp32 and
+ * multiplied by s_r, then the same fused prologue / epilogue runs. They
+ * stream half the weight bytes. K: 4096 (14336 for down_proj). */
+int cb_quantize_rows_i8(const void* w, int64_t rows, int K, void* q, float* scale, void* stream);
+int cb_qkv_rope_i8(const void* x, const void* norm_w, float eps, const void* wq, const float* sq,
+                   const void* wk, const float* sk, const void* wv, const float* sv, const float* inv_freq,
+                   const int32_t* position, int token, void* q_out, void* k_cache, void* v_cache,
+                   int64_t cache_len, int q_heads, int kv_heads, void* stream);
+int cb_proj_residual_i8(const void* x, int K, const void* w, const float* scale, int N, const void* residual,
+                        void* out, void* stream);
+int cb_gate_up_swiglu_i8(const void* x, const void* norm_w, float eps, const void* w_gate, const float* s_gate,
+                         const void* w_up, const float* s_up, int rows, void* out, void* stream);
+int cb_lm_head_topk_i8(const void* x, const void* norm_w, float eps, const void* w, const float* scale,
+                       int64_t rows, int64_t row_offset, int k, float* logits, float* out_values,
+                       int64_t* out_indices, void* workspace, unsigned int* ticket, void* stream);
 
 /* ------------------------------------------------------ tensor parallelism */
 

@@ -238,3 +238,116 @@ def _prefill_attention_case(ops, cuda, start, m, kv_heads, spike=False):
     ops.attention(q[0].transpose(0, 1).contiguous().view(m, -1), kc, vc, pos, 1, -(-length // 64) * 64, ref, ws,
                   tickets)
     torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.fixture
+def split_k(ops, cuda):
+    """Registers a split-K workspace for the test (and unregisters it)."""
+
+    from layer_streaming import _native
+
+    lib = _native.lib()
+    ws = torch.empty(48 << 18, dtype=torch.float32, device=cuda)  # 48 MB
+    tickets = torch.zeros(1024, dtype=torch.int32, device=cuda)
+    _native.check(lib.cb_set_gemm_workspace(ws.data_ptr(), 48 << 20, tickets.data_ptr(), 1024), "workspace")
+    try:
+        yield lib, tickets
+    finally:
+        lib.cb_set_gemm_workspace(None, 0, None, 0)
+
+
+def _unsplit(lib, fn):
+    lib.cb_set_gemm_workspace(None, 0, None, 0)
+    fn()
+
+
+@pytest.mark.parametrize("m", [1, 6, 16])
+def test_split_k_gemms_match_unsplit_and_torch(ops, cuda, split_k, m):
+    """Short chunks split each tile's K range over several CTAs; the last CTA
+    sums the fp32 slices in slice order and runs the same epilogue. The
+    outputs stay within one bf16 ulp of the unsplit kernel (a different fp32
+    summation order) and meet the torch criteria; the tickets return to 0."""
+
+    from layer_streaming import _native
+
+    lib, tickets = split_k
+    a = randn((m, 4096), 1500 + m, 1.0)
+    wo = randn((4096, 4096), 1501, 0.02)
+    wd = randn((4096, 14336), 1502, 0.02)
+    h = randn((m, 14336), 1503, 1.0)
+    res = randn((m, 4096), 1504, 1.0)
+    wg, wu = randn((14336, 4096), 1505, 0.02), randn((14336, 4096), 1506, 0.02)
+    wq, wk, wv = randn((4096, 4096), 1507, 0.02), randn((1024, 4096), 1508, 0.02), randn((1024, 4096), 1509, 0.02)
+    inv = lo.llama3_inv_freq(device=cuda)
+    pos = torch.tensor([3], dtype=torch.int32, device=cuda)
+    assert lib.cb_gemm_split_k(m, 14336, 4096, 0) == 9  # down: 32 tiles x 9 K slices
+    same_split = lib.cb_gemm_split_k(m, 4096, 14336, 1) == lib.cb_gemm_split_k(m, 4096, 14336, 0)
+    # the slice count depends on K alone; K = 4096 is not split (measured slower)
+    assert lib.cb_gemm_split_k(m, 4096, 4096, 0) == lib.cb_gemm_split_k(m, 4096, 6144, 0) == 1
+    assert lib.cb_gemm_split_k(17, 14336, 4096, 0) == 1  # longer chunks are not split
+
+    def run_all():
+        out = {}
+        out["o"] = torch.empty((m, 4096), dtype=BF16, device=cuda)
+        ops.gemm_residual(a, wo, res, out["o"])
+        out["down"] = torch.empty((m, 4096), dtype=BF16, device=cuda)
+        ops.gemm_residual(h, wd, res, out["down"])
+        out["bf16"] = torch.empty((m, 4096), dtype=BF16, device=cuda)
+        ops.gemm_bf16(a, wo, out["bf16"])
+        out["partial"] = torch.empty((m, 4096), dtype=torch.float32, device=cuda)
+        ops.gemm_partial(h, wd, out["partial"])
+        out["swiglu"] = torch.empty((m, 14336), dtype=BF16, device=cuda)
+        ops.gemm_swiglu(a, wg, wu, out["swiglu"])
+        out["silu_mul"] = torch.empty((m, 14336), dtype=BF16, device=cuda)
+        ops.gemm_silu(a, wg, out["silu_mul"])
+        ops.gemm_mul(a, wu, out["silu_mul"])
+        out["q"] = torch.empty((m, 4096), dtype=BF16, device=cuda)
+        out["kc"] = torch.full((8, m + 8, 128), 7.0, dtype=BF16, device=cuda)
+        out["vc"] = torch.full_like(out["kc"], 7.0)
+        ops.prefill_qkv_rope(a, wq, wk, wv, inv, pos, out["q"], out["kc"], out["vc"])
+        torch.cuda.synchronize()
+        return out
+
+    split = run_all()
+    assert int(tickets.abs().sum()) == 0
+    _unsplit(lib, lambda: None)
+    plain = run_all()
+
+    def proj_ulp(proj):
+        # one bf16 ulp of the largest projection value: the residual epilogue
+        # rounds the projection before the add, so when residual and
+        # projection cancel, a one-ulp flip of the projection is what the
+        # (small) output differs by
+        return 2.0 ** (torch.floor(torch.log2(proj.abs().max().float())).item() - 7)
+
+    # allowed difference from the unsplit kernel: one ulp of the projection
+    # (residual modes), two ulps of the output where two rounded values are
+    # combined (SwiGLU: silu(bf16 g) * bf16 u; RoPE: a difference of rounded
+    # products), one ulp of a plain store
+    ulp = {"o": proj_ulp(F.linear(a, wo)) + proj_ulp(plain["o"]),
+           "down": proj_ulp(F.linear(h, wd)) + proj_ulp(plain["down"]),
+           "bf16": proj_ulp(plain["bf16"]), "vc": proj_ulp(plain["vc"][:, 3:3 + m]),
+           "swiglu": 2 * proj_ulp(plain["swiglu"]), "silu_mul": 2 * proj_ulp(plain["silu_mul"]),
+           "q": 2 * proj_ulp(plain["q"]), "kc": 2 * proj_ulp(plain["kc"][:, 3:3 + m])}
+    for name in plain:
+        if name == "partial":
+            exact = h.double() @ wd.double().T
+            bound = 1e-6 * 14336 ** 0.5 * (h.double().abs() @ wd.double().abs().T) + 1e-6
+            assert bool(((split[name].double() - exact).abs() <= 8 * bound).all())
+            continue
+        got, ref = split[name].float(), plain[name].float()
+        assert (got - ref).abs().max().item() <= ulp[name], name
+        assert (got != ref).float().mean().item() <= 0.05, name
+    close_to_torch(split["bf16"], a, wo)
+    for name, proj in (("o", F.linear(a, wo)), ("down", F.linear(h, wd))):
+        ref = (res.float() + proj.float()).to(BF16).float()
+        assert (split[name].float() - ref).abs().max().item() <= ulp[name], name
+        assert (split[name].float() != ref).float().mean().item() <= 0.05, name
+    # the `matrix` granularity's gate / up GEMMs give the fused kernel's bits
+    # when both split K the same way (else: one fp32 summation order apart)
+    if same_split:
+        assert torch.equal(split["swiglu"], split["silu_mul"])
+    else:
+        assert (split["swiglu"].float() - split["silu_mul"].float()).abs().max().item() <= ulp["swiglu"]
+    outside = torch.cat([split["kc"][:, :3], split["kc"][:, 3 + m:]], dim=1)
+    assert bool((outside == 7.0).all())
