@@ -308,14 +308,17 @@ def time_e2e(executor, runtime, token, steps):
             "d2h_bytes_per_step": d2h}
 
 
-def time_streamed(plan, store, resident, executor, device, token, steps=3):
+def time_streamed(plan, store, resident, executor, device, token, steps=3, transfer="bf16"):
     """The reference's own mode on this GPU: every decode token streams the 15 GB
     of layer weights H2D from the pinned host arena through two 224 MiB slots
-    (copy stream overlapped with the compute stream), same kernels."""
+    (copy stream overlapped with the compute stream), same kernels. With
+    transfer="int8" the units cross PCIe as int8 rows + fp32 scales (about
+    half the bytes; reduced precision)."""
 
     import layer_streaming as ls
 
-    runtime = ls.DoubleBufferRuntime(plan, store, resident, device, weights="streamed", profile=True)
+    runtime = ls.DoubleBufferRuntime(plan, store, resident, device, weights="streamed", profile=True,
+                                     transfer=transfer)
     with torch.inference_mode():
         token = step(executor, runtime, token).topk_indices[..., 0]  # warm-up
         torch.cuda.synchronize()
@@ -329,7 +332,8 @@ def time_streamed(plan, store, resident, executor, device, token, steps=3):
     return {"ms_per_token": round(start.elapsed_time(end) / steps, 2), "steps": steps,
             "h2d_bytes_per_token": int(profile.get("h2d_bytes", plan.stream_bytes_per_token)),
             "h2d_effective_gbps": round(float(profile.get("h2d_effective_gbps", 0.0)), 2),
-            "note": "weights='streamed': H2D-bound (PCIe); the timed value is the HBM-resident mode"}
+            "note": "weights='streamed'{}: H2D-bound (PCIe); the timed value is the HBM-resident mode".format(
+                ", transfer='int8' (int8 rows + fp32 scales, reduced precision)" if transfer == "int8" else "")}
 
 
 def time_gate_up(executor, runtime, plan, reps=4):
@@ -985,7 +989,6 @@ def tensor_parallel(args, world, rank, local, device):
         },
         "cpu_baseline": None,
         "streamed_mode": streamed,
-        "int8_mode": int8,
         "prefill": {"tokens": args.context, "chunk": 512, "ms": round(prefill_ms, 2),
                     "tokens_per_s": round(args.context / (prefill_ms / 1000.0), 1)},
         "gpu_launches": (1 + 32 * 5 + 1 + 2) * args.steps if args.exchange == "peer" else None,
@@ -1049,6 +1052,9 @@ def main():
     e2e = time_e2e(executor, runtime, token, args.steps)
     gate_up_ms = time_gate_up(executor, runtime, plan)
     streamed = None if args.no_streamed else time_streamed(plan, store, resident, executor, device, token)
+    streamed_i8 = None
+    if not args.no_streamed and not args.no_int8:
+        streamed_i8 = time_streamed(plan, store, resident, executor, device, token, transfer="int8")
     int8 = None if args.no_int8 else time_int8(resident, runtime, device, args.context, args.steps, args.warmup)
     peak, peak_kind = measured_peak()
     context = executor.kv_cache.length - args.steps - 1  # mean cached length over the timed steps
@@ -1088,6 +1094,8 @@ def main():
         },
         "cpu_baseline": baseline,
         "streamed_mode": streamed,
+        "streamed_int8_mode": streamed_i8,
+        "int8_mode": int8,
         "prefill": {
             "tokens": args.context, "chunk": 512, "ms": round(prefill_ms, 2),
             "tokens_per_s": round(args.context / (prefill_ms / 1000.0), 1),

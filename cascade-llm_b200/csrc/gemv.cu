@@ -557,3 +557,38 @@ extern "C" int cb_lm_head_topk_i8(const void* x, const void* norm_w, float eps, 
   if (rc != kOk) return rc;
   return run_gemv<4096, true>("cb_lm_head_topk_i8", p, static_cast<cudaStream_t>(stream));
 }
+
+namespace cb {
+
+// bf16(q * scale) of int8 rows (the weights that prefill GEMMs use when a
+// unit arrives in int8): one thread per 8 weights.
+__global__ void __launch_bounds__(256) dequantize_rows_i8_kernel(const int8_t* __restrict__ q,
+                                                                 const float* __restrict__ scale, int64_t rows,
+                                                                 int K, uint16_t* __restrict__ out) {
+  const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (i >= rows * K) return;
+  const float s = __ldg(scale + i / K);
+  const uint2 v = *reinterpret_cast<const uint2*>(q + i);
+  const uint32_t w0 = v.x ^ 0x80808080u, w1 = v.y ^ 0x80808080u;
+  const float f[8] = {i8_at<0>(w0), i8_at<1>(w0), i8_at<2>(w0), i8_at<3>(w0),
+                      i8_at<0>(w1), i8_at<1>(w1), i8_at<2>(w1), i8_at<3>(w1)};
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) o[e] = uint32_t(f2bf(f[2 * e] * s)) | (uint32_t(f2bf(f[2 * e + 1] * s)) << 16);
+  *reinterpret_cast<uint4*>(out + i) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+}  // namespace cb
+
+extern "C" int cb_dequantize_rows_i8(const void* q, const float* scale, int64_t rows, int K, void* out,
+                                     void* stream) {
+  if (!q || !scale || !out || !aligned16(q) || !aligned16(out))
+    return fail(kErrInvalid, "cb_dequantize_rows_i8: q and out must be 16-byte aligned device pointers");
+  if (rows < 1 || K < 8 || K % 8) return fail(kErrInvalid, "cb_dequantize_rows_i8: rows >= 1, K a multiple of 8");
+  const int64_t threads = rows * K / 8;
+  const int64_t blocks = (threads + 255) / 256;
+  if (blocks > 0x7FFFFFFF) return fail(kErrInvalid, "cb_dequantize_rows_i8: too many weights");
+  dequantize_rows_i8_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const int8_t*>(q), scale, rows, K, static_cast<uint16_t*>(out));
+  return check_launch("cb_dequantize_rows_i8");
+}

@@ -54,6 +54,7 @@ _SIGNATURES = {
     "cb_lm_head_workspace_bytes": (_I64, [_I]),
     "cb_lm_head_topk": (_I, [_P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P, _P, _P, _P]),
     "cb_quantize_rows_i8": (_I, [_P, _I64, _I, _P, _P, _P]),
+    "cb_dequantize_rows_i8": (_I, [_P, _P, _I64, _I, _P, _P]),
     "cb_qkv_rope_i8": (_I, [_P, _P, _F, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _I64, _I, _I, _P]),
     "cb_proj_residual_i8": (_I, [_P, _I, _P, _P, _I, _P, _P, _P]),
     "cb_gate_up_swiglu_i8": (_I, [_P, _P, _F, _P, _P, _P, _P, _I, _P, _P]),

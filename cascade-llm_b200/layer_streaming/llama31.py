@@ -264,6 +264,7 @@ class Llama31DecodeExecutor:
         if self.decode_weights not in ("bf16", "int8"):
             raise ValueError("decode_weights must be 'bf16' or 'int8'")
         self._i8, self._i8_owner, self._i8_active, self._i8_step = {}, None, False, False
+        self._deq = None  # bf16 scratch of a unit that arrived as int8 (prefill)
         self._rows = 0
         self._buffers(1)
         self._attn_ws = None
@@ -465,11 +466,13 @@ class Llama31DecodeExecutor:
                 q8["lm_head.weight"] = (q, scale)
         self._i8, self._i8_owner = q8, id(runtime)
 
-    def _unit_i8(self, layer, operation, splits, chunk):
-        """One-token unit with int8 weights (the bf16 kernels' fused epilogues)."""
+    def _unit_i8(self, layer, operation, splits, chunk, weights8=None):
+        """One-token unit with int8 weights (the bf16 kernels' fused epilogues);
+        weights8: {key: (int8, scales)} (default: the HBM-resident quantized copy)."""
 
         cache, eps, pos, res = self.kv_cache, self.eps, self.kv_cache.position, self.resident
-        q8 = lambda name: self._i8[_matrix_key(layer, name)]
+        table = self._i8 if weights8 is None else weights8
+        q8 = lambda name: table[_matrix_key(layer, name)]
         kc, vc = cache.key(layer), cache.value(layer)
         if operation == "qkv":
             (wq, sq), (wk, sk), (wv, sv) = q8("q_proj"), q8("k_proj"), q8("v_proj")
@@ -540,11 +543,32 @@ class Llama31DecodeExecutor:
     def _embed_one(self):
         ops.embedding(self._ids_dev, self.resident["model.embed_tokens.weight"], self._x[:1])
 
+    def _dequantized(self, weights8):
+        """bf16 views of a unit that arrived as int8 rows (prefill GEMMs)."""
+
+        need = sum(q.numel() for q, _ in weights8.values())
+        if self._deq is None or self._deq.numel() < need:
+            self._deq = torch.empty(need, dtype=torch.bfloat16, device=self.device)
+        views, cursor = {}, 0
+        for key, (q, scale) in weights8.items():
+            out = self._deq.narrow(0, cursor, q.numel()).view(q.shape)
+            ops.dequantize_rows_i8(q, scale, out)
+            views[key] = out
+            cursor += q.numel()
+        return views
+
     def __call__(self, unit, weights, state):
         if self._embed_pending:
             self._embed_one()
             self._embed_pending = False
+        int8 = bool(weights) and isinstance(next(iter(weights.values())), tuple)  # streamed int8 transfer
+        if int8 and self._tokens > 1:
+            weights, int8 = self._dequantized(weights), False
         for operation in _UNIT_OPS.get(unit.operation, (unit.operation,)):
+            if int8:
+                splits, chunk, _ = self.attention_config(1, self.kv_cache.length + 1)
+                self._unit_i8(unit.layer_index, operation, splits, chunk, weights)
+                continue
             self._unit(unit.layer_index, operation, weights)
         if unit.layer_index == self.config.num_hidden_layers - 1 and unit.operation in ("layer", "down_proj"):
             self._after_last_unit()

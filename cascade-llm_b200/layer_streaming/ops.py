@@ -64,6 +64,7 @@ _SCHEMAS = {
     ),
     "position_advance": "position_advance(Tensor(a!) position, int count) -> ()",
     "quantize_rows_i8": "quantize_rows_i8(Tensor w, Tensor(a!) q, Tensor(b!) scale) -> ()",
+    "dequantize_rows_i8": "dequantize_rows_i8(Tensor q, Tensor scale, Tensor(a!) out) -> ()",
     "qkv_rope_i8": (
         "qkv_rope_i8(Tensor x, Tensor? norm_w, float eps, Tensor wq, Tensor sq, Tensor wk, Tensor sk, "
         "Tensor wv, Tensor sv, Tensor inv_freq, Tensor position, int token, Tensor(a!) q_out, "
@@ -417,6 +418,16 @@ def quantize_rows_i8(w, q, scale):
             _stream(w),
         ),
         "cascade.quantize_rows_i8",
+    )
+
+
+def dequantize_rows_i8(q, scale, out):
+    nat.check(
+        nat.lib().cb_dequantize_rows_i8(
+            nat.ptr(q, I8, "q"), nat.ptr(scale, F32, "scale"), q.shape[0], q.shape[1], nat.ptr(out, BF16, "out"),
+            _stream(q),
+        ),
+        "cascade.dequantize_rows_i8",
     )
 
 

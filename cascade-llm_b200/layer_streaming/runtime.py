@@ -19,6 +19,10 @@ keys), over two weight modes:
   unit is copied to HBM once at construction and ``run`` only launches
   compute; with this package's executor a one-token step is replayed as one
   captured CUDA graph.
+
+The streamed mode can also move its units as int8 rows with fp32 scales
+(``transfer="int8"`` or ``CASCADE_B200_TRANSFER=int8``: about half the PCIe
+bytes, reduced precision; :mod:`layer_streaming.int8_transfer`).
 """
 
 import os
@@ -32,6 +36,7 @@ from .plan import ModelPlan
 from .streaming import SlotRing
 
 WEIGHT_MODES = ("streamed", "hbm")
+TRANSFER_FORMATS = ("bf16", "int8")
 
 
 @dataclass
@@ -117,11 +122,14 @@ class DoubleBufferRuntime:
 
     ``weights`` selects ``"streamed"`` (the reference's behaviour, default)
     or ``"hbm"`` (all units resident in device memory); ``None`` reads
-    ``CASCADE_B200_WEIGHTS``.
+    ``CASCADE_B200_WEIGHTS``. ``transfer`` (streamed mode) selects ``"bf16"``
+    units (the reference's) or ``"int8"`` units (int8 rows + fp32 scales,
+    handed to ``compute_unit`` as ``{key: (int8, scales)}``); ``None`` reads
+    ``CASCADE_B200_TRANSFER``.
     """
 
     def __init__(self, plan, store, resident, device="cuda:0", slot_count=None, profile=False,
-                 weights=None):
+                 weights=None, transfer=None):
         self.device = _cuda_device(device)
         self.plan = plan
         self.store = store
@@ -129,6 +137,12 @@ class DoubleBufferRuntime:
         self.weights = str(weights or os.environ.get("CASCADE_B200_WEIGHTS", "streamed")).lower()
         if self.weights not in WEIGHT_MODES:
             raise ValueError("weights must be one of {}".format(WEIGHT_MODES))
+        self.transfer = str(transfer or os.environ.get("CASCADE_B200_TRANSFER", "bf16")).lower()
+        if self.transfer not in TRANSFER_FORMATS:
+            raise ValueError("transfer must be one of {}".format(TRANSFER_FORMATS))
+        if self.transfer == "int8" and self.weights != "streamed":
+            raise ValueError("transfer='int8' is the streamed mode's (HBM-resident int8: the executor's "
+                             "decode_weights='int8')")
         self.slot_count = plan.slot_count if slot_count is None else int(slot_count)
         if self.slot_count not in (1, 2):
             raise ValueError("slot_count must be 1 or 2")
@@ -143,10 +157,17 @@ class DoubleBufferRuntime:
         self.compute_stream = torch.cuda.Stream(device=self.device)
         self.coordinator = torch.cuda.current_stream(self.device)
         self.unit_arena = None
+        self.int8_arena = None
         self._views = None
         self._ring = None
         if self.weights == "hbm":
             self._load_units()
+        elif self.transfer == "int8":
+            from .int8_transfer import Int8UnitArena
+
+            self.int8_arena = Int8UnitArena(plan, store, self.device)
+            self._views = [self.int8_arena.views(i, self.device_slots[i % slots]) for i in range(len(plan.units))]
+            self._ring = SlotRing(self.device_slots, self.copy_stream)  # the int8 arena is pinned
         else:
             self._views = [_piece_views(unit, self.device_slots[i % slots]) for i, unit in enumerate(plan.units)]
             staging = store.staging_buffers() if hasattr(store, "staging_buffers") else None
@@ -234,16 +255,18 @@ class DoubleBufferRuntime:
 
         if hasattr(self.store, "reset_profile"):
             self.store.reset_profile()
-        numbers = self._ring.run(self.store.unit_spans(units), body, self.compute_stream, self.coordinator,
-                                 profile=self.profile)
+        spans = self.int8_arena.spans() if self.int8_arena is not None else self.store.unit_spans(units)
+        numbers = self._ring.run(spans, body, self.compute_stream, self.coordinator, profile=self.profile)
         if self.profile:
             profile = {key: numbers[key] for key in (
                 "wall_ms", "host_submit_ms", "source_wait_ms", "gpu_pipeline_ms", "h2d_event_sum_ms",
                 "compute_event_sum_ms")}
             moved = self.plan.stream_bytes_per_token
+            if self.int8_arena is not None:
+                moved += self.int8_arena.nbytes - 2 * sum(unit.elements for unit in units)
             profile["h2d_bytes"] = moved
             profile["h2d_effective_gbps"] = (moved / 1e9) / max(numbers["h2d_event_sum_ms"] / 1000.0, 1e-12)
-            if self.store.mode == "pinned_staging":
+            if self.store.mode == "pinned_staging" and self.int8_arena is None:
                 for key in ("staging_copy_count", "staging_event_sum_ms", "staging_event_max_ms"):
                     profile[key] = numbers[key]
             self.last_profile = profile

@@ -332,6 +332,10 @@ int cb_set_prefill_attention_tc(int enable);
  * multiplied by s_r, then the same fused prologue / epilogue runs. They
  * stream half the weight bytes. K: 4096 (14336 for down_proj). */
 int cb_quantize_rows_i8(const void* w, int64_t rows, int K, void* q, float* scale, void* stream);
+/* out = bf16(q * scale) row by row: the bf16 weights that the prefill GEMMs
+ * use when a unit arrives in int8 (the streamed int8 transfer). q: int8
+ * [rows, K] (16-byte aligned); out: bf16 [rows, K]; K a multiple of 8. */
+int cb_dequantize_rows_i8(const void* q, const float* scale, int64_t rows, int K, void* out, void* stream);
 int cb_qkv_rope_i8(const void* x, const void* norm_w, float eps, const void* wq, const float* sq,
                    const void* wk, const float* sk, const void* wv, const float* sv, const float* inv_freq,
                    const int32_t* position, int token, void* q_out, void* k_cache, void* v_cache,

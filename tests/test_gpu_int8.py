@@ -192,3 +192,56 @@ def test_int8_engine_tracks_the_bf16_engine(cuda, hbm_engine, meta):
         print("int8 vs bf16: logits cosine {:.5f}, top-10 overlap {}/10, top-1 {} / {}".format(
             cos, overlap, int(i8[0]), int(ib[0])))
         assert cos > 0.98
+
+
+def test_streamed_int8_transfer(cuda, arena, hbm_engine, meta):
+    """The reference's streamed mode with int8 units (transfer='int8'): about
+    half the H2D bytes per token; its one-token steps give the bits of the
+    HBM-resident int8 executor (same quantized weights, same kernels), and a
+    multi-token prompt (prefill GEMMs on dequantized units) tracks the bf16
+    engine within the quantization noise."""
+
+    import layer_streaming as ls
+
+    from conftest import Config, make_store
+
+    plan = ls.build_llama31_8b_plan("matrix_group")
+    store = make_store(arena, plan)
+    resident = ls.ResidentDeviceArena(plan, store, cuda)
+    streamed = ls.DoubleBufferRuntime(plan, store, resident, cuda, weights="streamed", transfer="int8", profile=True)
+    _, _, hbm_resident, hbm_runtime = hbm_engine
+
+    def run(executor, runtime, prompt, steps, forced=None):
+        """Per step (top-k, logits, the residual stream after the last layer)."""
+
+        out = []
+        with torch.inference_mode():
+            ids = prompt
+            for step in range(steps):
+                state = executor.finish(runtime.run(executor, executor.begin(ids)))
+                out.append((state.topk_indices.clone(), state.logits.clone(), executor._x[0].clone()))
+                ids = state.topk_indices[..., 0].reshape(1, 1) if forced is None else forced[step].view(1, 1)
+        executor.check_errors()
+        return out
+
+    # every step one token: both paths run the int8 GEMVs on identical int8
+    # layer weights, so the residual stream after the 32 layers is the same
+    # bits (the HBM int8 executor also quantizes its resident LM head, the
+    # streamed transfer only the layer units, so the logits differ)
+    first = torch.tensor([[meta["prompt_ids"][0]]], dtype=torch.int64, device=cuda)
+    forced = torch.tensor(meta["prompt_ids"][1:5], dtype=torch.int64, device=cuda)
+    got = run(ls.Llama31DecodeExecutor(Config(), resident, top_k=10), streamed, first, 4, forced)
+    ref = run(ls.Llama31DecodeExecutor(Config(), hbm_resident, top_k=10, decode_weights="int8"), hbm_runtime,
+              first, 4, forced)
+    for (_, _, h1), (_, _, h2) in zip(got, ref):
+        assert torch.equal(h1, h2)
+    moved = streamed.last_profile["h2d_bytes"]
+    assert abs(moved - streamed.int8_arena.nbytes) == 0
+    assert 0.49 < moved / plan.stream_bytes_per_token < 0.51
+    # a 6-token prompt: prefill on dequantized units, then int8 one-token steps
+    ids = torch.tensor(meta["prompt_ids"], dtype=torch.int64, device=cuda).view(1, -1)
+    got = run(ls.Llama31DecodeExecutor(Config(), resident, top_k=10), streamed, ids, 3)
+    ref = run(ls.Llama31DecodeExecutor(Config(), hbm_resident, top_k=10), hbm_runtime, ids, 3)
+    cos = F.cosine_similarity(got[0][1].view(-1).double(), ref[0][1].view(-1).double(), dim=0).item()
+    print("streamed int8 prefill vs bf16: logits cosine {:.5f}".format(cos))
+    assert cos > 0.98
