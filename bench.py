@@ -438,11 +438,17 @@ def micro_gemm(args, device):
 
     from layer_streaming import _native, ops
 
-    _native.check(_native.lib().cb_prepare(), "cb_prepare")
+    lib = _native.lib()
+    _native.check(lib.cb_prepare(), "cb_prepare")
     bf = torch.bfloat16
     name = args.micro
     n, k = GEMM_SHAPES[name]
     m = args.tokens
+    # the executor's split-K registration for short chunks
+    split_ws = torch.empty(4 << 20, dtype=torch.float32, device=device)
+    split_tickets = torch.zeros(1024, dtype=torch.int32, device=device)
+    _native.check(lib.cb_set_gemm_workspace(split_ws.data_ptr(), 16 << 20, split_tickets.data_ptr(), 1024),
+                  "cb_set_gemm_workspace")
     gen = torch.Generator(device=device).manual_seed(5)
     a = (torch.randn((m, k), generator=gen, device=device)).to(bf)
     layers = 8
@@ -478,7 +484,10 @@ def micro_gemm(args, device):
     flops = 2.0 * m * n * k
     tflops = flops / (us * 1e-6) / 1e12
     peak, kind = measured_peak("bf16_tflops")
-    print(json.dumps({"micro": name, "tokens": m, "us_per_launch": round(us, 3), "flop_per_launch": flops,
+    k_split = lib.cb_gemm_split_k(m, k, n // 2 if name == "gemm_gate_up" else n, 1 if name == "gemm_gate_up" else 0)
+    lib.cb_set_gemm_workspace(None, 0, None, 0)
+    print(json.dumps({"micro": name, "tokens": m, "k_split": k_split, "us_per_launch": round(us, 3),
+                      "flop_per_launch": flops,
                       "achieved_tflops": round(tflops, 1), "peak_tflops": peak, "peak_kind": kind,
                       "frac": round(tflops / peak, 4), "weight_gbs": round(n * k * 2 / (us * 1e-6) / 1e9, 1),
                       "launches": launches}), flush=True)
