@@ -128,7 +128,8 @@ def test_split_swiglu_and_single_matrix_qkv_equal_the_fused_gemms(ops, cuda):
     assert torch.equal(q2, q) and torch.equal(kc2, kc) and torch.equal(vc2, vc)
 
 
-@pytest.mark.parametrize("start,m,q_heads,kv_heads", [(0, 6, 32, 8), (100, 128, 32, 8), (7, 200, 8, 2)])
+@pytest.mark.parametrize("start,m,q_heads,kv_heads", [(0, 6, 32, 8), (100, 128, 32, 8), (7, 200, 8, 2),
+                                                     (5, 1100, 32, 8)])
 def test_prefill_qkv_rope_matches_decode_kernel(ops, cuda, start, m, q_heads, kv_heads):
     xn = randn((m, 4096), 1300 + m, 1.0)
     wq = randn((q_heads * 128, 4096), 1301, 0.02)
