@@ -166,6 +166,39 @@ def test_eager_and_graph_replay_are_identical(cuda, hbm_engine, meta):
         assert torch.equal(v1, v2) and torch.equal(i1, i2) and torch.equal(l1, l2)
 
 
+def test_l2_staging_is_only_a_cache_hint(cuda, hbm_engine, meta):
+    """The attention launches prefetch part of the layer's gate+up weights into
+    L2 (on by default); with every kind of staging switched off, or with the
+    QKV and o_proj launches staging too, the decode steps give the same bits."""
+
+    import layer_streaming as ls
+    from layer_streaming import _native
+
+    lib = _native.lib()
+    _, _, resident, runtime = hbm_engine
+    ids = prompt_ids(6, seed=meta["prompt_seed"]).view(1, -1).to(cuda)
+    settings = {
+        "default": [],
+        "off": [(1, 0, 0, 0, 0)],
+        "all kinds": [(0, 3, 4, 4, 0), (2, 1, 4, 8, 0), (1, 3, 10, 12, 1)],
+    }
+    runs = {}
+    try:
+        for name, knobs in settings.items():
+            lib.cb_set_l2_stage(1, 3, 10, 4, 0)  # the default
+            for knob in knobs:
+                _native.check(lib.cb_set_l2_stage(*knob), "cb_set_l2_stage")
+            executor = ls.Llama31DecodeExecutor(Config(), resident, top_k=meta["top_k"], return_full_logits=True)
+            runs[name] = generate(executor, runtime, ids, 4)
+    finally:
+        lib.cb_set_l2_stage(0, 0, 0, 0, 0)
+        lib.cb_set_l2_stage(1, 3, 10, 4, 0)
+        lib.cb_set_l2_stage(2, 0, 0, 0, 0)
+    for name in ("off", "all kinds"):
+        for (v1, i1, l1), (v2, i2, l2) in zip(runs["default"], runs[name]):
+            assert torch.equal(v1, v2) and torch.equal(i1, i2) and torch.equal(l1, l2), name
+
+
 def test_resident_head_returns_last_token_logits(cuda, hbm_engine, meta):
     """Like the reference's resident head (llama31.py:330-339), ``finish``
     fills ``state.logits`` without being asked: the last token's fp32 row,
