@@ -48,7 +48,9 @@ enum GemmMode : int {
 };
 
 constexpr int kBM = 128;
-constexpr int kSplitMaxTokens = 16;  // split-K chunks: the reduced tile [M][BN] fits shared memory
+// split-K chunks: the reduced tile [M][BN] fp32 fits shared memory next to
+// the ring (64 x 128 or 16 x 256 floats, 32 / 16 KB)
+constexpr int split_max_tokens(int BN) { return BN == 128 ? 64 : 16; }
 constexpr int kMaxSplit = 9;
 constexpr int kBK = 64;
 constexpr int kStages = 4;
@@ -70,7 +72,7 @@ struct GemmParams {
   uint16_t* v_cache;
   int64_t cache_len;
   int* err;
-  // split-K (M <= 16 rows, too few tiles for the SMs): the K blocks of a
+  // split-K (M <= 64 rows with 128-wide tiles, too few tiles for the SMs): the K blocks of a
   // tile are split over `ksplit` work items; each stores its fp32 partial
   // rows into `ws` [tile][ksplit][M][BN], and the last item of a tile to
   // finish (acq_rel ticket) sums them in slice order into shared memory and
@@ -87,8 +89,8 @@ struct GemmSmem {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int BAR = kStages * STAGE;                 // full[S], empty[S], acc_full[2], acc_empty[2]
   static constexpr int TMEM_SLOT = BAR + (2 * kStages + 4) * 8;
-  static constexpr int RED = TMEM_SLOT + 16;                  // split-K: the reduced tile [M <= 16][BN] fp32
-  static constexpr int BYTES = RED + 16 * BN * 4 + 1024;      // + slack to align the ring to 1024 B
+  static constexpr int RED = TMEM_SLOT + 16;                  // split-K: the reduced tile [M][BN] fp32
+  static constexpr int BYTES = RED + split_max_tokens(BN) * BN * 4 + 1024;  // + slack to align the ring
   static_assert(BYTES <= 227 * 1024, "GEMM shared memory");
 };
 
@@ -465,7 +467,8 @@ int64_t g_splitk_bytes = 0;
 unsigned int* g_splitk_tickets = nullptr;
 int g_splitk_ntickets = 0;
 
-// K slices per tile: 1, unless the chunk is short (M <= 16: one M tile,
+// K slices per tile: 1, unless the chunk is short (M <= 64 with 128-wide
+// tiles, M <= 16 with 256-wide ones: one M tile,
 // fewer tiles than SMs) and K is long (>= 8192: the down projection's
 // 14336, 9 slices, 32 tiles -> 288 work items). The count depends on K
 // alone, so every projection with the same K sums the same fp32 slices in
@@ -475,7 +478,7 @@ int g_splitk_ntickets = 0;
 // 74 us, gate+up 70 -> 87, o_proj 32.5 -> 32 with 5 slices). A workspace
 // too small for the launch means no split.
 int choose_ksplit(int M, int K, int tiles, int BN) {
-  if (!g_splitk_ws || M > kSplitMaxTokens || tiles >= sm_count() || tiles > g_splitk_ntickets) return 1;
+  if (!g_splitk_ws || M > split_max_tokens(BN) || tiles >= sm_count() || tiles > g_splitk_ntickets) return 1;
   if (K / kBK < 128) return 1;
   const int S = kMaxSplit;
   if (K / kBK / S < 4) return 1;

@@ -51,7 +51,7 @@ _UNIT_OPS = {
 _TOPK_MAX = 64
 # prefill chunks of at most this many tokens split the GEMMs' K range (one
 # 128-row tile leaves most SMs idle); workspace and per-tile tickets
-_SPLIT_K_MAX_TOKENS = 16
+_SPLIT_K_MAX_TOKENS = 64
 _SPLIT_K_BYTES = 16 << 20
 _SPLIT_K_TICKETS = 1024
 _DEFAULT_CAPACITY = 8192

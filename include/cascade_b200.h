@@ -267,7 +267,8 @@ int cb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache
  *                        caches [kv_heads, cache_len, 128] (K after RoPE); any of
  *                        wq / wk / wv may be NULL (the `matrix` granularity) */
 int cb_gemm_bf16(const void* a, int M, int K, const void* w, int N, void* out, void* stream);
-/* Split-K for short chunks (M <= 16, fewer output tiles than SMs, e.g. a
+/* Split-K for short chunks (M <= 64 with 128-wide output tiles, M <= 16 with
+ * 256-wide ones; fewer output tiles than SMs, e.g. a
  * 6-token prompt: 32 down_proj tiles on 148 SMs): registers the fp32
  * workspace and the zeroed per-tile tickets that the prefill GEMMs above use
  * to split a tile's K range into 9 slices when K >= 8192 (the down

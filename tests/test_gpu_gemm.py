@@ -262,7 +262,7 @@ def _unsplit(lib, fn):
     fn()
 
 
-@pytest.mark.parametrize("m", [1, 6, 16])
+@pytest.mark.parametrize("m", [1, 6, 16, 64])
 def test_split_k_gemms_match_unsplit_and_torch(ops, cuda, split_k, m):
     """Short chunks split each tile's K range over several CTAs; the last CTA
     sums the fp32 slices in slice order and runs the same epilogue. The
@@ -285,7 +285,7 @@ def test_split_k_gemms_match_unsplit_and_torch(ops, cuda, split_k, m):
     same_split = lib.cb_gemm_split_k(m, 4096, 14336, 1) == lib.cb_gemm_split_k(m, 4096, 14336, 0)
     # the slice count depends on K alone; K = 4096 is not split (measured slower)
     assert lib.cb_gemm_split_k(m, 4096, 4096, 0) == lib.cb_gemm_split_k(m, 4096, 6144, 0) == 1
-    assert lib.cb_gemm_split_k(17, 14336, 4096, 0) == 1  # longer chunks are not split
+    assert lib.cb_gemm_split_k(65, 14336, 4096, 0) == 1  # longer chunks are not split
 
     def run_all():
         out = {}
