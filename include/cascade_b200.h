@@ -251,7 +251,7 @@ int cb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache
 /* Prefill projections of an M-token chunk on the tcgen05 tensor cores
  * (BF16 in, FP32 accumulate in TMEM, bf16 out): the F.linear calls of
  * llama31.py:238-280 with M > 1. A / xn: [M, K] row-major activations; W:
- * [N, K] row-major weights; K a multiple of 64; all pointers 16-byte
+ * [N, K] row-major weights; K a multiple of 128; all pointers 16-byte
  * aligned. Rounding points are those of the decode kernels.
  *   cb_gemm_bf16:        out[M, N] = bf16(A . W^T); N a multiple of 128
  *   cb_gemm_residual:    out = bf16(residual + bf16(A . W^T)) (out may be residual)
