@@ -98,6 +98,8 @@ def parse_args():
     parser.add_argument("--context", type=int, default=2048)
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--tokens", type=int, default=512, help="rows of the --micro gemm_* cases")
+    parser.add_argument("--prefill-chunk", type=int, default=2048,
+                        help="tokens per prefill step of the context fill (the prefill line's chunk)")
     parser.add_argument("--sweep", action="store_true",
                         help="BASELINE config 3: each projection at M in {1, 6, 64, 512}, HBM-resident and "
                              "H2D-streamed through two slots (one JSON line per case)")
@@ -1040,7 +1042,7 @@ def main():
 
     extra = args.warmup + args.steps * 2 + 72
     plan, store, resident, runtime, executor = build_engine(device, args.context, extra)
-    token, prefill_ms = prefill(executor, runtime, device, args.context)
+    token, prefill_ms = prefill(executor, runtime, device, args.context, chunk=args.prefill_chunk)
     if args.profile_range:
         with torch.inference_mode():
             for _ in range(args.warmup):
@@ -1106,7 +1108,7 @@ def main():
         "streamed_int8_mode": streamed_i8,
         "int8_mode": int8,
         "prefill": {
-            "tokens": args.context, "chunk": 512, "ms": round(prefill_ms, 2),
+            "tokens": args.context, "chunk": args.prefill_chunk, "ms": round(prefill_ms, 2),
             "tokens_per_s": round(args.context / (prefill_ms / 1000.0), 1),
             "note": "first (cold) prefill through the API: tcgen05 GEMMs + split-KV attention per chunk",
         },

@@ -120,7 +120,7 @@ def compare(engine_steps, oracle_steps, label, noise):
     print("{}: engine greedy ids {}".format(label, [int(i[0]) for _, i in engine_steps]))
 
 
-@pytest.mark.parametrize("context,chunk,decode_steps", [(2048, 512, 8), (4096, 512, 4)])
+@pytest.mark.parametrize("context,chunk,decode_steps", [(2048, 512, 8), (4096, 512, 4), (4096, 2048, 4)])
 def test_chunked_prefill_then_decode_matches_single_shot(cuda, hbm_engine, reference_noise, context, chunk,
                                                          decode_steps):
     """2048 ids in 4 x 512 chunks + 8 decode steps (exactly what bench.py
