@@ -35,6 +35,7 @@ for _p in (ROOT, os.path.join(ROOT, "cascade-llm_b200")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "decode ms/token, Llama-3.1-8B arch bs=1 (2K ctx)"
@@ -110,6 +111,9 @@ def parse_args():
     parser.add_argument("--profile-range", action="store_true",
                         help="after warm-up, run --steps decode steps between cudaProfilerStart/Stop "
                              "(for `ncu --profile-from-start off`) and exit")
+    parser.add_argument("--trace", action="store_true",
+                        help="after warm-up, record the per-CTA %%globaltimer timeline (cb_set_trace) of "
+                             "--steps decode steps and print per-kernel-role phase medians as JSON, then exit")
     parser.add_argument("--micro",
                         choices=sorted(MICRO_BYTES) + sorted(GEMM_SHAPES) + ["prefill_attention", "exchange"],
                         help="time one kernel alone on a small footprint (rotating copies > L2)")
@@ -259,6 +263,91 @@ def time_decode(executor, runtime, token, steps, warmup, barrier):
         torch.cuda.synchronize()
         barrier()
     return start.elapsed_time(end) / steps, token
+
+
+TRACE_ROLES = ("qkv", "attention", "o_proj", "gate_up", "down_proj")
+
+
+def trace_decode(executor, runtime, token, steps, warmup):
+    """Per-CTA launch timeline of `steps` decode steps (cb_set_trace).
+
+    Each traced CTA records its start, the return of its dependency wait,
+    the end of its main loop (attention: of its sub-chunk loop) and its end
+    (%globaltimer ns); the LM head also the end of its own top-k and of its
+    ticket. Launches are grouped per step in issue order (per layer QKV,
+    attention, o_proj, gate+up, down; then the LM head). Reported per role,
+    as medians over layers and steps, in us: `interval` from the previous
+    launch's last CTA end to this launch's last CTA end, `wait_release` from
+    the previous launch's end to this launch's first released wait, `loop`
+    from its last released wait to its last main-loop end, `loop_spread`
+    between its first and last main-loop end, and `tail` from the last
+    main-loop end to the last CTA end."""
+
+    from layer_streaming import _native
+
+    lib = _native.lib()
+    per_step = 32 * 1500 + 400  # 32 x (4 GEMV grids of 296 CTAs + 256 attention CTAs) + the LM head
+    cap = per_step * steps
+    buf = torch.zeros(8 * (cap + 1), dtype=torch.int64, device=executor.device)
+    buf[1] = cap
+    _native.check(lib.cb_set_trace(buf.data_ptr()), "cb_set_trace")
+    executor._graphs.clear()  # recapture: a captured launch keeps the trace pointer it was captured with
+    try:
+        with torch.inference_mode():
+            for _ in range(warmup):
+                token = step(executor, runtime, token).topk_indices[..., 0]
+            torch.cuda.synchronize()
+            buf[0] = 0
+            for _ in range(steps):
+                token = step(executor, runtime, token).topk_indices[..., 0]
+            torch.cuda.synchronize()
+    finally:
+        _native.check(lib.cb_set_trace(None), "cb_set_trace")
+        executor._graphs.clear()
+    count = min(int(buf[0].item()), cap)
+    rec = buf[8:8 * (count + 1)].view(count, 8).cpu().numpy()
+    tags = rec[:, 0] >> 32
+    launches = []
+    for tag in np.unique(tags):
+        rows = rec[tags == tag]
+        rows = rows[np.argsort(rows[:, 2])]
+        # a captured launch replays its tag once per step: split at gaps of > 0.5 ms
+        cuts = np.where(np.diff(rows[:, 2]) > 500_000)[0] + 1
+        launches.extend(np.split(rows, cuts))
+    launches.sort(key=lambda r: int(r[:, 2].min()))
+    layer_launches = 5 * 32
+    roles = {name: {"interval": [], "wait_release": [], "loop": [], "loop_spread": [], "tail": []}
+             for name in TRACE_ROLES + ("lm_head",)}
+    head_phases = {"topk": [], "ticket": [], "merge": []}
+    spans = []
+    i = 0
+    while i + layer_launches < len(launches):
+        group = launches[i:i + layer_launches + 1]
+        i += layer_launches + 1
+        prev_end = None
+        for j, r in enumerate(group):
+            name = TRACE_ROLES[j % 5] if j < layer_launches else "lm_head"
+            end, wait_min, wait_max = r[:, 5].max(), r[:, 3].min(), r[:, 3].max()
+            loop_min, loop_max = r[:, 4].min(), r[:, 4].max()
+            d = roles[name]
+            if prev_end is not None:
+                d["interval"].append((end - prev_end) / 1e3)
+                d["wait_release"].append((wait_min - prev_end) / 1e3)
+            d["loop"].append((loop_max - wait_max) / 1e3)
+            d["loop_spread"].append((loop_max - loop_min) / 1e3)
+            d["tail"].append((end - loop_max) / 1e3)
+            prev_end = end
+        head = group[-1]
+        head_phases["topk"].append((head[:, 6].max() - head[:, 4].max()) / 1e3)
+        head_phases["ticket"].append((head[:, 7].max() - head[:, 6].max()) / 1e3)
+        head_phases["merge"].append((head[:, 5].max() - head[:, 7].max()) / 1e3)
+        spans.append((group[-1][:, 5].max() - group[0][:, 2].min()) / 1e3)
+    med = lambda v: round(float(np.median(v)), 2) if v else None
+    return {"trace": "decode step, per-CTA %globaltimer", "context": executor.kv_cache.length, "steps": len(spans),
+            "step_us": [round(x, 1) for x in spans],
+            "roles_us": {name: {k: med(v) for k, v in d.items()} for name, d in roles.items()},
+            "lm_head_tail_us": {k: med(v) for k, v in head_phases.items()},
+            "note": "tracing adds a few %globaltimer reads and one atomic per CTA; compare shares"}
 
 
 def time_int8(resident, runtime, device, context, steps, warmup):
@@ -1043,6 +1132,9 @@ def main():
     extra = args.warmup + args.steps * 2 + 72
     plan, store, resident, runtime, executor = build_engine(device, args.context, extra)
     token, prefill_ms = prefill(executor, runtime, device, args.context, chunk=args.prefill_chunk)
+    if args.trace:
+        print(json.dumps(trace_decode(executor, runtime, token, args.steps, args.warmup)), flush=True)
+        return
     if args.profile_range:
         with torch.inference_mode():
             for _ in range(args.warmup):
