@@ -178,6 +178,40 @@ def test_lm_head_topk(ops, cuda, rows, offset, k):
     assert int(ticket.item()) == 0
 
 
+@pytest.mark.parametrize("patterns,k", [(1, 10), (1, 64), (3, 10), (7, 64)])
+def test_lm_head_topk_massive_ties(ops, cuda, patterns, k):
+    """A head whose rows repeat `patterns` distinct rows: every logit takes
+    one of `patterns` values, so every CTA's candidate list ties with every
+    other's and the selection rests on the row-id rule alone (smaller id
+    first). Covers the merge that loads all candidates into registers (k=10)
+    and the threshold-filter merge (k=64) under the ties that bf16 logits
+    produce."""
+
+    rows = 128256
+    x = randn((4096,), 42)
+    norm_w = torch.ones(4096, dtype=BF16, device=cuda)
+    base = randn((patterns, 4096), 43, 0.02)
+    w = base.repeat((rows + patterns - 1) // patterns, 1)[:rows].contiguous()
+    logits = torch.empty(rows, dtype=torch.float32, device=cuda)
+    values = torch.empty(k, dtype=torch.float32, device=cuda)
+    indices = torch.empty(k, dtype=torch.int64, device=cuda)
+    ws = torch.full((ops.lm_head_workspace_bytes(k),), 0xAB, dtype=torch.uint8, device=cuda)
+    ticket = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for _ in range(2):
+        ops.lm_head_topk(x, norm_w, 1e-5, w, 0, k, logits, values, indices, ws, ticket)
+        # identical rows give identical logits
+        assert torch.equal(logits.view(-1, 1)[:patterns * (rows // patterns)].view(-1, patterns),
+                           logits[:patterns].expand(rows // patterns, patterns))
+        ov, oi = _topk_oracle(logits, k)
+        assert torch.equal(values.cpu(), ov)
+        assert torch.equal(indices.cpu(), oi)
+    best = int(torch.argmax(logits[:patterns]).item()) if patterns > 1 else 0
+    if int((logits[:patterns] == logits[best]).sum()) == 1:
+        # one pattern holds the maximum: the k smallest ids of that pattern
+        assert indices.cpu().tolist() == [best + patterns * i for i in range(k)]
+    assert int(ticket.item()) == 0
+
+
 def test_topk_merge_with_ties(ops, cuda):
     gen = torch.Generator().manual_seed(5)
     a_v = torch.randint(0, 20, (37,), generator=gen).float()
