@@ -208,7 +208,7 @@ __device__ __forceinline__ void warp_topk_regs(const uint32_t* keys, IdOf id_of,
 // (missing entries: -inf, INT64_MAX). Not inlined, so that the LM head's
 // last-CTA merge runs the same instructions as every CTA's own top-k just
 // before it instead of code that no warp of the SM has fetched yet.
-static __device__ __noinline__ void stage_topk(const uint32_t* stage, int k, float* out_v, int64_t* out_i) {
+static __device__ __noinline__ void stage_topk(uint32_t* stage, int k, float* out_v, int64_t* out_i) {
   constexpr int W = kThreads / 32;
   const uint32_t* ids = stage + W * k;
   auto to_out = [out_v, out_i](int r, uint32_t key, uint32_t id) {
@@ -221,7 +221,7 @@ static __device__ __noinline__ void stage_topk(const uint32_t* stage, int k, flo
   else if (W * k <= 128)
     warp_topk_regs<4>(stage, stage_id, 0, W * k, k, to_out);
   else
-    warp_topk(const_cast<uint32_t*>(stage), stage_id, 0, W * k, k, to_out);
+    warp_topk(stage, stage_id, 0, W * k, k, to_out);
 }
 
 // Exact top-k of n entries (keys in shared memory, ids by id_of) by the whole
