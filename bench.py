@@ -306,6 +306,15 @@ def trace_decode(executor, runtime, token, steps, warmup):
         executor._graphs.clear()
     count = min(int(buf[0].item()), cap)
     rec = buf[8:8 * (count + 1)].view(count, 8).cpu().numpy()
+    summary = summarize_trace(rec)
+    summary["context"] = executor.kv_cache.length
+    return summary
+
+
+def summarize_trace(rec, layers=32):
+    """Phase medians of trace records (rows of 8 int64 words as cb_set_trace
+    writes them) of whole decode steps; see trace_decode for the phases."""
+
     tags = rec[:, 0] >> 32
     launches = []
     for tag in np.unique(tags):
@@ -315,7 +324,7 @@ def trace_decode(executor, runtime, token, steps, warmup):
         cuts = np.where(np.diff(rows[:, 2]) > 500_000)[0] + 1
         launches.extend(np.split(rows, cuts))
     launches.sort(key=lambda r: int(r[:, 2].min()))
-    layer_launches = 5 * 32
+    layer_launches = len(TRACE_ROLES) * layers
     roles = {name: {"interval": [], "wait_release": [], "loop": [], "loop_spread": [], "tail": []}
              for name in TRACE_ROLES + ("lm_head",)}
     head_phases = {"topk": [], "ticket": [], "merge": []}
@@ -326,7 +335,7 @@ def trace_decode(executor, runtime, token, steps, warmup):
         i += layer_launches + 1
         prev_end = None
         for j, r in enumerate(group):
-            name = TRACE_ROLES[j % 5] if j < layer_launches else "lm_head"
+            name = TRACE_ROLES[j % len(TRACE_ROLES)] if j < layer_launches else "lm_head"
             end, wait_min, wait_max = r[:, 5].max(), r[:, 3].min(), r[:, 3].max()
             loop_min, loop_max = r[:, 4].min(), r[:, 4].max()
             d = roles[name]
@@ -343,7 +352,7 @@ def trace_decode(executor, runtime, token, steps, warmup):
         head_phases["merge"].append((head[:, 5].max() - head[:, 7].max()) / 1e3)
         spans.append((group[-1][:, 5].max() - group[0][:, 2].min()) / 1e3)
     med = lambda v: round(float(np.median(v)), 2) if v else None
-    return {"trace": "decode step, per-CTA %globaltimer", "context": executor.kv_cache.length, "steps": len(spans),
+    return {"trace": "decode step, per-CTA %globaltimer", "steps": len(spans),
             "step_us": [round(x, 1) for x in spans],
             "roles_us": {name: {k: med(v) for k, v in d.items()} for name, d in roles.items()},
             "lm_head_tail_us": {k: med(v) for k, v in head_phases.items()},
